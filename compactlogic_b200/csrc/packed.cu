@@ -1,0 +1,332 @@
+// Bit-packed discrete inference: 64 samples per uint64 word, one argmax gate per neuron.
+//
+// Activations are [features, words] with bit i of word w holding sample 64*w + i (LSB first), the
+// bit order of the reference's tensor_packbits_cuda (compactlogic/cuda/difflogic_kernel.cu:434-449).
+// Because that order is little-endian, a row packed into 8/16/32/64-bit words has the same bytes
+// for every width; only the row length is rounded to the word width.
+//
+// A layer evaluates one gate per neuron on whole words (gates.cuh gate_word, a branch-free
+// multiplexer over the truth-table bits), so one 8-byte load per operand yields 64 gate-evals.
+// GroupSum on packed words (groupbitsum, difflogic_kernel.cu:500-533) is a per-bit-position
+// ("vertical") population count over the neurons of a class; it is computed with a Harley-Seal
+// carry-save adder tree over 16 words at a time (about 4 logic ops per word instead of 64 bit
+// tests), and the final layer can be fused with it so its outputs are never stored.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "gates.cuh"
+#include "kernels.h"
+
+namespace clb {
+
+namespace {
+
+// ------------------------------------------------------------------------------------------
+// Harley-Seal vertical counter: 64 independent counters, one per bit position.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void csa(uint64_t& h, uint64_t& l, uint64_t a, uint64_t b, uint64_t c) {
+    const uint64_t u = a ^ b;
+    h = (a & b) | (u & c);
+    l = u ^ c;
+}
+
+struct VCounter {
+    static constexpr int kPlanes = 20;  // counts of 16-word groups up to 2^20 - 1
+    uint64_t ones = 0, twos = 0, fours = 0, eights = 0;
+    uint64_t hi[kPlanes];
+    __device__ __forceinline__ VCounter() {
+#pragma unroll
+        for (int p = 0; p < kPlanes; ++p) hi[p] = 0;
+    }
+    // Add 16 words.
+    __device__ __forceinline__ void add16(const uint64_t (&d)[16]) {
+        uint64_t twosA, twosB, foursA, foursB, eightsA, eightsB, sixteens;
+        csa(twosA, ones, ones, d[0], d[1]);
+        csa(twosB, ones, ones, d[2], d[3]);
+        csa(foursA, twos, twos, twosA, twosB);
+        csa(twosA, ones, ones, d[4], d[5]);
+        csa(twosB, ones, ones, d[6], d[7]);
+        csa(foursB, twos, twos, twosA, twosB);
+        csa(eightsA, fours, fours, foursA, foursB);
+        csa(twosA, ones, ones, d[8], d[9]);
+        csa(twosB, ones, ones, d[10], d[11]);
+        csa(foursA, twos, twos, twosA, twosB);
+        csa(twosA, ones, ones, d[12], d[13]);
+        csa(twosB, ones, ones, d[14], d[15]);
+        csa(foursB, twos, twos, twosA, twosB);
+        csa(eightsB, fours, fours, foursA, foursB);
+        csa(sixteens, eights, eights, eightsA, eightsB);
+        uint64_t carry = sixteens;
+#pragma unroll
+        for (int p = 0; p < kPlanes; ++p) {
+            const uint64_t t = hi[p] & carry;
+            hi[p] ^= carry;
+            carry = t;
+        }
+    }
+    __device__ __forceinline__ int value(int i) const {
+        int v = (int)((ones >> i) & 1) + 2 * (int)((twos >> i) & 1) + 4 * (int)((fours >> i) & 1) +
+                8 * (int)((eights >> i) & 1);
+        int h = 0;
+#pragma unroll
+        for (int p = 0; p < kPlanes; ++p) h |= (int)((hi[p] >> i) & 1) << p;
+        return v + 16 * h;
+    }
+};
+
+// Load 8 bytes of a packed row at byte offset `off`, zero beyond `row_bytes`.
+__device__ __forceinline__ uint64_t load_word_bytes(const uint8_t* __restrict__ row, int64_t off, int64_t row_bytes,
+                                                    bool aligned8) {
+    if (aligned8 && off + 8 <= row_bytes) return *reinterpret_cast<const uint64_t*>(row + off);
+    uint64_t v = 0;
+    for (int b = 0; b < 8; ++b)
+        if (off + b < row_bytes) v |= (uint64_t)row[off + b] << (8 * b);
+    return v;
+}
+
+// Flush a counter for word column w into counts[(sample0 + 64 w + i) * k + c], i < 64.
+__device__ __forceinline__ void flush_counts(const VCounter& vc, int64_t w, int64_t c, int64_t k, int64_t samples,
+                                             int32_t* __restrict__ counts, int64_t sample0) {
+    for (int i = 0; i < 64; ++i) {
+        const int64_t n = 64 * w + i;
+        if (n >= samples) break;
+        const int v = vc.value(i);
+        if (v) atomicAdd(counts + (sample0 + n) * k + c, v);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// tensor_packbits: bool [rows, cols] -> little-endian packed rows of `row_bytes` bytes.
+// One warp per 32 samples of one row: the ballot of the 32 bools is the 4 packed bytes.
+// ------------------------------------------------------------------------------------------
+__global__ void packbits_kernel(const uint8_t* __restrict__ t, int64_t rows, int64_t cols, int64_t ld_t,
+                                uint8_t* __restrict__ out, int64_t row_bytes) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nblk = (row_bytes + 3) / 4;
+    const int64_t total = rows * nblk;
+    for (int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < total;
+         e += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const int64_t r = e / nblk, blk = e - r * nblk;
+        const int64_t c = blk * 32 + lane;
+        const bool bit = c < cols && t[r * ld_t + c] != 0;
+        const uint32_t word = __ballot_sync(0xffffffffu, bit);
+        if (lane < 4) {
+            const int64_t byte = blk * 4 + lane;
+            if (byte < row_bytes) out[r * row_bytes + byte] = (uint8_t)(word >> (8 * lane));
+        }
+    }
+}
+
+// groupbitsum: counts[n, c] += sum over rows of class c of bit n.  One thread per
+// (class, segment of rows, 64-sample word column); lanes run over word columns.
+__global__ void groupbitsum_kernel(const uint8_t* __restrict__ words, int64_t rows, int64_t row_bytes,
+                                   int64_t samples, int64_t k, int64_t class_size, int64_t nseg, int64_t seg_len,
+                                   int32_t* __restrict__ counts, int64_t sample0) {
+    const int64_t W = (row_bytes + 7) / 8;
+    const int64_t total = k * nseg * W;
+    const bool al8 = (row_bytes % 8) == 0 && ((uintptr_t)words % 8) == 0;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t w = e % W;
+        const int64_t cs = e / W;
+        const int64_t seg = cs % nseg, c = cs / nseg;
+        const int64_t r0 = c * class_size + seg * seg_len;
+        const int64_t r1 = min(min(r0 + seg_len, (c + 1) * class_size), rows);
+        VCounter vc;
+        for (int64_t r = r0; r < r1; r += 16) {
+            uint64_t d[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                d[q] = (r + q < r1) ? load_word_bytes(words + (r + q) * row_bytes, 8 * w, row_bytes, al8) : 0ull;
+            vc.add16(d);
+        }
+        flush_counts(vc, w, c, k, samples, counts, sample0);
+    }
+}
+
+// pack_inputs: x [batch, features] (sample-major, values in {0,1}; bit = x > 0.5)
+//           -> out [features, ldw] uint64, bit i of word w = sample 64 w + i.
+template <typename T>
+__global__ void pack_inputs_kernel(const T* __restrict__ x, int64_t batch, int64_t features, int64_t ldx,
+                                   uint64_t* __restrict__ out, int64_t ldw) {
+    __shared__ uint8_t tile[64][33];
+    const int64_t s0 = (int64_t)blockIdx.y * 64, f0 = (int64_t)blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 64; i += blockDim.y) {
+        const int64_t s = s0 + i, f = f0 + threadIdx.x;
+        uint8_t b = 0;
+        if (s < batch && f < features) b = to_acc(x[s * ldx + f]) > 0.5f;
+        tile[i][threadIdx.x] = b;
+    }
+    __syncthreads();
+    if (threadIdx.y < 2) {
+        const int64_t f = f0 + threadIdx.x;
+        uint32_t half = 0;
+        for (int i = 0; i < 32; ++i) half |= (uint32_t)tile[threadIdx.y * 32 + i][threadIdx.x] << i;
+        if (f < features) reinterpret_cast<uint32_t*>(out + f * ldw + blockIdx.y)[threadIdx.y] = half;
+    }
+}
+
+__global__ void packed_select_kernel(const int2* __restrict__ slots, const uint8_t* __restrict__ gates,
+                                     const uint8_t* __restrict__ select, int64_t n_out, int K, int64_t group,
+                                     int2* __restrict__ sel_ab, uint8_t* __restrict__ sel_gate) {
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n_out; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = j / group;
+        const int k = select[r];
+        if (k < K) {
+            sel_ab[j] = slots[j * K + k];
+            sel_gate[j] = gates[r * K + k] & 15;
+        } else {  // invalid selection: constant-0 gate
+            sel_ab[j] = make_int2(-1, -1);
+            sel_gate[j] = 0;
+        }
+    }
+}
+
+__device__ __forceinline__ uint64_t word_or_zero(const uint64_t* __restrict__ x, int idx, int64_t ldx, int64_t w) {
+    return idx >= 0 ? __ldg(x + (int64_t)idx * ldx + w) : 0ull;
+}
+
+// One packed layer.  TW lanes span word columns, 32/TW neurons per warp.
+__global__ void __launch_bounds__(256)
+packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
+                    const uint8_t* __restrict__ sel_gate, int64_t n_out, uint64_t* __restrict__ y, int64_t ldy,
+                    int tw_log2) {
+    const int TW = 1 << tw_log2;
+    const int lane = threadIdx.x & 31;
+    const int64_t w = (int64_t)blockIdx.x * TW + (lane & (TW - 1));
+    const int64_t npw = 32 >> tw_log2;  // neurons per warp
+    const int64_t warp_global = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) >> 5;
+    const int64_t stride = ((int64_t)gridDim.y * blockDim.x >> 5) * npw;
+    if (w >= nwords) return;
+    for (int64_t j = warp_global * npw + (lane >> tw_log2); j < n_out; j += stride) {
+        const int2 ab = sel_ab[j];
+        const int g = sel_gate[j];
+        const uint64_t a = word_or_zero(x, ab.x, ldx, w);
+        const uint64_t b = word_or_zero(x, ab.y, ldx, w);
+        y[j * ldy + w] = gate_word<uint64_t>(g, a, b);
+    }
+}
+
+// Final packed layer fused with the packed GroupSum: computes each neuron's word and feeds it
+// straight into the vertical counter of its class, never storing the layer output.
+__global__ void __launch_bounds__(256)
+packed_layer_count_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
+                          const uint8_t* __restrict__ sel_gate, int64_t n_out, int64_t k, int64_t class_size,
+                          int64_t nseg, int64_t seg_len, int32_t* __restrict__ counts, int64_t sample0,
+                          int64_t samples) {
+    const int64_t total = k * nseg * nwords;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t w = e % nwords;
+        const int64_t cs = e / nwords;
+        const int64_t seg = cs % nseg, c = cs / nseg;
+        const int64_t j0 = c * class_size + seg * seg_len;
+        const int64_t j1 = min(min(j0 + seg_len, (c + 1) * class_size), n_out);
+        VCounter vc;
+        for (int64_t j = j0; j < j1; j += 16) {
+            uint64_t d[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                uint64_t v = 0;
+                if (j + q < j1) {
+                    const int2 ab = sel_ab[j + q];
+                    v = gate_word<uint64_t>(sel_gate[j + q], word_or_zero(x, ab.x, ldx, w),
+                                            word_or_zero(x, ab.y, ldx, w));
+                }
+                d[q] = v;
+            }
+            vc.add16(d);
+        }
+        flush_counts(vc, w, c, k, samples, counts, sample0);
+    }
+}
+
+unsigned grid_for(int64_t threads) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(threads, 256), (int64_t)148 * 32));
+}
+
+// Enough (class, segment, word) threads to fill the GPU, segments of at least 64 rows.
+void choose_segments(int64_t k, int64_t class_size, int64_t W, int64_t& nseg, int64_t& seg_len) {
+    const int64_t target = 148 * 2048;
+    nseg = std::max<int64_t>(1, std::min<int64_t>(ceil_div64(class_size, 64), ceil_div64(target, std::max<int64_t>(1, k * W))));
+    seg_len = ceil_div64(class_size, nseg);
+    nseg = ceil_div64(class_size, seg_len);
+}
+
+}  // namespace
+
+cudaError_t launch_packbits(const uint8_t* t, int64_t rows, int64_t cols, int64_t ld_t, int bits, uint8_t* out,
+                            int64_t row_bytes, cudaStream_t s) {
+    (void)bits;
+    if (rows == 0 || row_bytes == 0) return cudaSuccess;
+    const int64_t warps = rows * ((row_bytes + 3) / 4);
+    packbits_kernel<<<grid_for(warps * 32), 256, 0, s>>>(t, rows, cols, ld_t, out, row_bytes);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_groupbitsum(const uint8_t* words, int64_t rows, int64_t row_bytes, int64_t samples, int64_t k,
+                               int64_t class_size, int32_t* counts, bool accumulate, int64_t sample0,
+                               cudaStream_t s) {
+    if (!accumulate) {
+        cudaError_t e = cudaMemsetAsync(counts + sample0 * k, 0, sizeof(int32_t) * samples * k, s);
+        if (e != cudaSuccess) return e;
+    }
+    if (rows == 0 || samples == 0 || k == 0) return cudaSuccess;
+    const int64_t W = (row_bytes + 7) / 8;
+    int64_t nseg, seg_len;
+    choose_segments(k, class_size, W, nseg, seg_len);
+    groupbitsum_kernel<<<grid_for(k * nseg * W), 256, 0, s>>>(words, rows, row_bytes, samples, k, class_size, nseg,
+                                                              seg_len, counts, sample0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx,
+                               uint64_t* out, int64_t ldw, cudaStream_t s) {
+    if (batch == 0 || features == 0) return cudaSuccess;
+    dim3 grid((unsigned)ceil_div64(features, 32), (unsigned)ceil_div64(batch, 64));
+    dim3 block(32, 8);
+    switch (dtype) {
+        case CLB_F32: pack_inputs_kernel<float><<<grid, block, 0, s>>>((const float*)x, batch, features, ldx, out, ldw); break;
+        case CLB_F64: pack_inputs_kernel<double><<<grid, block, 0, s>>>((const double*)x, batch, features, ldx, out, ldw); break;
+        case CLB_BF16: pack_inputs_kernel<__nv_bfloat16><<<grid, block, 0, s>>>((const __nv_bfloat16*)x, batch, features, ldx, out, ldw); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_packed_select(const int32_t* slots, const uint8_t* gates, const uint8_t* select, int64_t n_out,
+                                 int K, int64_t group, int32_t* sel_ab, uint8_t* sel_gate, cudaStream_t s) {
+    if (n_out == 0) return cudaSuccess;
+    packed_select_kernel<<<grid_for(n_out), 256, 0, s>>>(reinterpret_cast<const int2*>(slots), gates, select, n_out, K,
+                                                         group, reinterpret_cast<int2*>(sel_ab), sel_gate);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
+                                const uint8_t* sel_gate, int64_t n_out, uint64_t* y, int64_t ldy, cudaStream_t s) {
+    if (n_out == 0 || nwords == 0) return cudaSuccess;
+    int tw_log2 = 0;
+    while ((1 << tw_log2) < nwords && tw_log2 < 5) ++tw_log2;
+    const int64_t TW = 1 << tw_log2;
+    const int64_t npw = 32 / TW;
+    const int64_t warps_needed = ceil_div64(n_out, npw);
+    const int64_t by = std::min<int64_t>(ceil_div64(warps_needed, 8), 65535);
+    dim3 grid((unsigned)ceil_div64(nwords, TW), (unsigned)by);
+    packed_layer_kernel<<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate, n_out, y,
+                                             ldy, tw_log2);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
+                                      const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size,
+                                      int32_t* counts, int64_t sample0, int64_t nsamples, cudaStream_t s) {
+    if (n_out == 0 || nwords == 0 || k == 0) return cudaSuccess;
+    int64_t nseg, seg_len;
+    choose_segments(k, class_size, nwords, nseg, seg_len);
+    packed_layer_count_kernel<<<grid_for(k * nseg * nwords), 256, 0, s>>>(
+        x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate, n_out, k, class_size, nseg, seg_len, counts,
+        sample0, nsamples);
+    return cudaGetLastError();
+}
+
+}  // namespace clb

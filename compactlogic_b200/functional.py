@@ -1,0 +1,133 @@
+"""Autograd functions of the native fast path (softmax, gate mix, GroupSum and their backward fused
+into the sm_100a kernels).
+
+Activations live feature-major, ``[features, batch]`` contiguous, as in the reference dense kernels
+(compactlogic/cuda/difflogic_kernel.cu:8-12); a layer's public output is the transposed view, so a
+chain of layers never copies (compactlogic/compactlogic.py:101-118 uses the same convention).
+"""
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+
+@dataclass
+class LayerSpec:
+    """Device-side description of one logic layer (a slot table plus its per-row parameters)."""
+    slots: torch.Tensor          # int32 [n_out, K, 2]
+    gates: torch.Tensor          # uint8 [n_out/group, K]
+    n_out: int
+    K: int
+    group: int
+    in_features: int
+    has_pad: bool
+
+
+def _check_x(xt: torch.Tensor, spec: LayerSpec) -> None:
+    L.require_cuda(xt)
+    if xt.dim() != 2 or xt.shape[0] != spec.in_features or xt.stride(1) != 1:
+        raise RuntimeError(f"expected feature-major activations [{spec.in_features}, batch] with unit column stride, "
+                           f"got shape {tuple(xt.shape)} strides {xt.stride()}")
+
+
+def forward_into(xt: torch.Tensor, weights: Optional[torch.Tensor], spec: LayerSpec, mode: int,
+                 select: Optional[torch.Tensor] = None, y: Optional[torch.Tensor] = None,
+                 gs_acc: Optional[torch.Tensor] = None, gs_size: int = 0) -> None:
+    _check_x(xt, spec)
+    B = xt.shape[1]
+    L.call("clb_logic_forward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
+           spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), L.ptr(select), int(spec.has_pad), L.ptr(y),
+           y.stride(0) if y is not None else 0, L.ptr(gs_acc), gs_acc.shape[0] if gs_acc is not None else 0, gs_size,
+           gs_acc.stride(0) if gs_acc is not None else 0, L.stream(xt.device))
+
+
+def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode: int,
+                  gy: Optional[torch.Tensor], gs_grad: Optional[torch.Tensor], gs_size: int, gs_scale: float,
+                  need_gx: bool, need_gw: bool):
+    """Returns (grad_x [in, B] or None, grad_weights [rows, K] or None)."""
+    B = xt.shape[1]
+    acc = L.acc_dtype(xt.dtype)
+    dev = xt.device
+    gx = torch.empty(spec.in_features, B, dtype=acc, device=dev) if need_gx else None
+    gy_ptr, ldgy = (L.ptr(gy), gy.stride(0)) if gy is not None else (0, 0)
+    gs_ptr, ld_gs, gs_k = (L.ptr(gs_grad), gs_grad.stride(0), gs_grad.shape[0]) if gs_grad is not None else (0, 0, 0)
+    part = None
+    chunks = 0
+    if need_gw:
+        chunks = int(L.lib().clb_logic_backward_chunks(L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, gy_ptr,
+                                                       ldgy, gs_ptr, ld_gs, L.ptr(gx), B))
+        part = torch.empty(max(chunks, 1), spec.n_out, spec.K, dtype=acc, device=dev)
+    L.call("clb_logic_backward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
+           spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), int(spec.has_pad), gy_ptr, ldgy, gs_ptr, gs_k,
+           gs_size, ld_gs, float(gs_scale), L.ptr(gx), B, 1, spec.in_features, L.ptr(part), chunks,
+           L.stream(dev))
+    gw = None
+    if need_gw:
+        gw = torch.empty(spec.n_out // spec.group, spec.K, dtype=acc, device=dev)
+        L.call("clb_logic_grad_finalize", L.dtype_code(xt.dtype), L.ptr(part), chunks if B > 0 else 0, spec.n_out,
+               spec.K, spec.group, mode, L.ptr(weights), L.ptr(gw), L.stream(dev))
+    return gx, gw
+
+
+class LogicLayerFn(torch.autograd.Function):
+    """y [n_out, B] = soft logic layer of xt [in, B] with gate logits `weights` [rows, K].
+
+    Fuses the reference's ``softmax(weights)`` (compactlogic/compactlogic.py:108), the kernel
+    forward (difflogic_kernel.cu:39-78) and, in backward, grad_x, grad_w and the softmax backward
+    (compactlogic.py:488-508 + torch autograd)."""
+
+    @staticmethod
+    def forward(ctx, xt, weights, spec: LayerSpec):
+        y = torch.empty(spec.n_out, xt.shape[1], dtype=xt.dtype, device=xt.device)
+        forward_into(xt, weights, spec, L.W_LOGITS, y=y)
+        ctx.save_for_backward(xt, weights)
+        ctx.spec = spec
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        xt, weights = ctx.saved_tensors
+        spec = ctx.spec
+        gy = gy.to(L.acc_dtype(xt.dtype))
+        if gy.stride(1) != 1 or gy.stride(0) < gy.shape[1]:
+            gy = gy.contiguous()
+        gx, gw = backward_into(xt, weights, spec, L.W_LOGITS, gy, None, 0, 1.0, ctx.needs_input_grad[0],
+                               ctx.needs_input_grad[1])
+        return gx, gw, None
+
+
+class LogicGroupSumFn(torch.autograd.Function):
+    """Last logic layer with GroupSum fused (compactlogic/compactlogic.py:450-468): returns the raw
+    class sums [k, B]; the layer output [n_out, B] is never materialised, and the backward
+    synthesises grad_y[j, n] = grad[class(j), n] on the fly."""
+
+    @staticmethod
+    def forward(ctx, xt, weights, spec: LayerSpec, k: int, gs_size: int):
+        acc = torch.zeros(k, xt.shape[1], dtype=L.acc_dtype(xt.dtype), device=xt.device)
+        forward_into(xt, weights, spec, L.W_LOGITS, gs_acc=acc, gs_size=gs_size)
+        ctx.save_for_backward(xt, weights)
+        ctx.spec, ctx.gs_size = spec, gs_size
+        return acc
+
+    @staticmethod
+    def backward(ctx, gacc):
+        xt, weights = ctx.saved_tensors
+        gacc = gacc.contiguous().to(L.acc_dtype(xt.dtype))
+        gx, gw = backward_into(xt, weights, ctx.spec, L.W_LOGITS, None, gacc, ctx.gs_size, 1.0,
+                               ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+        return gx, gw, None, None, None
+
+
+def eval_forward(xt: torch.Tensor, spec: LayerSpec, select: torch.Tensor) -> torch.Tensor:
+    """Discrete float eval (difflogic_kernel.cu:341-369): y [n_out, B]."""
+    y = torch.empty(spec.n_out, xt.shape[1], dtype=xt.dtype, device=xt.device)
+    forward_into(xt, None, spec, L.W_SELECT, select=select, y=y)
+    return y
+
+
+def eval_group_sum(xt: torch.Tensor, spec: LayerSpec, select: torch.Tensor, k: int, gs_size: int) -> torch.Tensor:
+    acc = torch.zeros(k, xt.shape[1], dtype=L.acc_dtype(xt.dtype), device=xt.device)
+    forward_into(xt, None, spec, L.W_SELECT, select=select, gs_acc=acc, gs_size=gs_size)
+    return acc

@@ -1,0 +1,130 @@
+"""Bit-packed discrete inference of a CompactLogic network.
+
+The reference evaluates a trained network in eval mode with one argmax gate per neuron applied to
+fp32 activations (compactlogic/compactlogic.py:120-130, compactlogic/cuda/difflogic_kernel.cu:341-369)
+and recovers class counts as round(logits * tau) (simulation/paper_stats.py:56).  Here the same
+network runs on bits: 64 samples per uint64 word, one gate evaluation per word, and the final
+layer is fused with a per-class vertical popcount, producing the exact integer class counts.
+
+Samples are processed in chunks of ``chunk_words`` words (64 samples each): all layers of one chunk
+run back to back so the chunk's intermediate activations (n_out x chunk_words x 8 bytes per layer)
+stay in the 126 MB L2 instead of round-tripping through HBM.
+"""
+from typing import List, Optional
+
+import torch
+
+from . import _lib as L
+from .compactlogic import ConvLayer, GroupSum, LogicLayer
+
+
+class _Frozen:
+    __slots__ = ("sel_ab", "sel_gate", "n_out", "in_features")
+
+    def __init__(self, sel_ab, sel_gate, n_out, in_features):
+        self.sel_ab, self.sel_gate, self.n_out, self.in_features = sel_ab, sel_gate, n_out, in_features
+
+
+class PackedLogicNet:
+    """Discrete packed-inference engine for ``Sequential(LogicLayer|ConvLayer|Flatten ..., GroupSum)``.
+
+    forward(x) -> int32 class counts [batch, k]; logits(x) = counts / tau, equal to the reference
+    eval-mode output; predict(x) = argmax (first maximum, as torch.argmax).
+    """
+
+    def __init__(self, model: torch.nn.Module, device=None, chunk_words: int = 32):
+        mods = list(model)
+        if not mods or not isinstance(mods[-1], GroupSum):
+            raise ValueError("PackedLogicNet needs a model ending in GroupSum")
+        gs = mods[-1]
+        self.k, self.tau = int(gs.k), float(gs.tau)
+        self.device = torch.device(device) if device is not None else mods[0].weights.device
+        self.chunk_words = int(chunk_words)
+        self.layers: List[_Frozen] = []
+        for m in mods[:-1]:
+            if isinstance(m, torch.nn.Flatten):
+                continue
+            if not isinstance(m, LogicLayer):
+                raise ValueError(f"PackedLogicNet: unsupported module {type(m).__name__}")
+            self.layers.append(self._freeze_tables(m))
+        if not self.layers:
+            raise ValueError("PackedLogicNet: no logic layers")
+        for prev, nxt in zip(self.layers[:-1], self.layers[1:]):
+            if prev.n_out != nxt.in_features:
+                raise ValueError("PackedLogicNet: layer widths do not chain")
+        self.in_features = self.layers[0].in_features
+        self.class_size = -(-self.layers[-1].n_out // self.k)
+        self._bufs = None
+
+    @torch.no_grad()
+    def _freeze_tables(self, layer: LogicLayer) -> _Frozen:
+        spec = layer._layer_spec(self.device)
+        sel = layer._selected().to(self.device)
+        n_out = spec.n_out
+        sel_ab = torch.empty(n_out, 2, dtype=torch.int32, device=self.device)
+        sel_gate = torch.empty(n_out, dtype=torch.uint8, device=self.device)
+        L.call("clb_packed_select", L.ptr(spec.slots), L.ptr(spec.gates), L.ptr(sel.contiguous()), n_out, spec.K,
+               spec.group, L.ptr(sel_ab), L.ptr(sel_gate), L.stream(self.device))
+        in_features = spec.in_features
+        return _Frozen(sel_ab, sel_gate, n_out, in_features)
+
+    # ------------------------------------------------------------------
+    def pack(self, x: torch.Tensor) -> torch.Tensor:
+        """[batch, features] (or [batch, C, H, W]) {0,1} -> [features, ceil(batch/64)] uint64."""
+        x = x.reshape(x.shape[0], -1)
+        if x.dtype not in (torch.float32, torch.float64, torch.bfloat16):
+            x = x.to(torch.float32)
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        B, F = x.shape
+        if F != self.in_features:
+            raise ValueError(f"expected {self.in_features} input features, got {F}")
+        W = -(-B // 64)
+        xw = torch.empty(F, W, dtype=torch.int64, device=self.device)
+        L.call("clb_pack_inputs", L.dtype_code(x.dtype), L.ptr(x), B, F, x.stride(0), L.ptr(xw), W,
+               L.stream(self.device))
+        return xw
+
+    def _buffers(self, width: int):
+        if self._bufs is None or self._bufs[0].shape[1] < width:
+            rows = max(l.n_out for l in self.layers[:-1]) if len(self.layers) > 1 else 1
+            self._bufs = tuple(torch.empty(rows, width, dtype=torch.int64, device=self.device) for _ in range(2))
+        return self._bufs
+
+    @torch.no_grad()
+    def counts_packed(self, xw: torch.Tensor, batch: int, counts: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Class counts [batch, k] of pre-packed inputs xw [features, W]."""
+        W = xw.shape[1]
+        if counts is None:
+            counts = torch.zeros(batch, self.k, dtype=torch.int32, device=self.device)
+        else:
+            counts.zero_()
+        cw = max(1, min(self.chunk_words, W))
+        bufs = self._buffers(cw)
+        s = L.stream(self.device)
+        for w0 in range(0, W, cw):
+            nw = min(cw, W - w0)
+            src, ld_src = xw[:, w0:], W
+            for li, layer in enumerate(self.layers[:-1]):
+                dst = bufs[li % 2]
+                L.call("clb_packed_layer", L.ptr(src), ld_src, nw, L.ptr(layer.sel_ab), L.ptr(layer.sel_gate),
+                       layer.n_out, L.ptr(dst), dst.stride(0), s)
+                src, ld_src = dst, dst.stride(0)
+            last = self.layers[-1]
+            nsamp = min(64 * nw, batch - 64 * w0)
+            L.call("clb_packed_layer_count", L.ptr(src), ld_src, nw, L.ptr(last.sel_ab), L.ptr(last.sel_gate),
+                   last.n_out, self.k, self.class_size, L.ptr(counts), 64 * w0, nsamp, s)
+        return counts
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        L.require_cuda(x)
+        return self.counts_packed(self.pack(x), x.shape[0])
+
+    __call__ = forward
+
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        return self.forward(x).to(torch.float32) / self.tau
+
+    def predict(self, x: torch.Tensor) -> torch.Tensor:
+        return self.forward(x).argmax(-1)

@@ -1,0 +1,238 @@
+/*
+ * compactlogic_b200 — C ABI of the B200 (sm_100a) CompactLogic logic-layer hot path.
+ *
+ * Conventions
+ *   - Every pointer argument is a device pointer unless its name ends in `_host`.
+ *   - Every buffer is allocated by the caller.  No entry point allocates device memory; entry points
+ *     that need temporary device memory take a caller-provided `workspace` and have a matching
+ *     `*_workspace_bytes` query.
+ *   - `stream` is a cudaStream_t (pass the caller's current stream; 0 = legacy default stream).
+ *     All work is enqueued asynchronously on it.  Entry points marked (sync) read a device flag
+ *     back and so synchronise with the stream.
+ *   - Return value: CLB_OK or a CLB_ERR_* code; clb_last_error() gives a message for the calling
+ *     thread.  No entry point ever terminates the process (the reference aborts via exit() on a CUDA
+ *     error, compactlogic/cuda/utils.cuh:46-53).
+ *   - Activations are feature-major: x[feature][column] with row stride `ld` elements (the
+ *     reference dense layout, compactlogic/cuda/difflogic_kernel.cu:8-12), unless stated otherwise.
+ *
+ * Two groups of entry points:
+ *   1. clb_difflogic_* / clb_convlogic_* / clb_tensor_packbits / clb_groupbitsum mirror, one to one,
+ *      the functions of the reference's pybind modules `difflogic_cuda` and `convlogic_cuda`
+ *      (compactlogic/cuda/difflogic.cpp:60-105, compactlogic/cuda/convlogic.cpp:49-110), with the
+ *      same tensor layouts, argument meaning and results.
+ *   2. clb_logic_* / clb_slots_* / clb_packed_* are the native fast path used by the Python layers
+ *      (softmax and its backward fused, int32 slot tables, fused GroupSum, bit-packed inference).
+ */
+#ifndef COMPACTLOGIC_B200_H
+#define COMPACTLOGIC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* clb_stream_t; /* cudaStream_t */
+
+enum clb_status {
+    CLB_OK = 0,
+    CLB_ERR_INVALID = 1,      /* bad shape / size / null pointer / unsupported option */
+    CLB_ERR_DTYPE = 2,        /* unsupported element type */
+    CLB_ERR_INDEX = 3,        /* a connection index or offset points outside the input */
+    CLB_ERR_CUDA = 4,         /* a CUDA launch or runtime call failed */
+    CLB_ERR_WORKSPACE = 5,    /* workspace too small */
+    CLB_ERR_DIVISIBILITY = 6  /* groupbitsum: rows not divisible by k (reference raises ValueError) */
+};
+
+enum clb_dtype { CLB_F32 = 0, CLB_F64 = 1, CLB_BF16 = 2 };
+
+/* How a layer's per-row weights are interpreted. */
+enum clb_weight_mode {
+    CLB_W_LOGITS = 0, /* raw gate logits; softmax over K taken in-kernel (compactlogic.py:108) */
+    CLB_W_PROBS = 1,  /* probabilities, as the reference kernels receive them */
+    CLB_W_SELECT = 2  /* discrete: one chosen slot per row (`select`), gate output unweighted */
+};
+
+const char* clb_last_error(void);
+int clb_abi_version(void);
+/* Number of kernels this library launched since load (host-side counter, all threads). */
+long long clb_launch_count(void);
+
+/* ============================== 1. reference-mirroring entry points ==============================
+ * Dtypes: the reference dispatches fp32/fp64(/fp16) for dense and fp32/fp64 for conv; here fp32 and
+ * fp64 are accepted (fp16 is not).  Indices a, b are int64 [out_dim, K] (the two halves of the
+ * layer's `indices` buffer), gate_seq uint8 [out_dim, K], w [out_dim, K] in the activation dtype.
+ */
+
+/* Replaces difflogic_cuda.forward(x, a, b, w, gate_seq) -> y  (compactlogic/cuda/difflogic.cpp:61-66,
+ * compactlogic/cuda/difflogic_kernel.cu:197-236).  x [in_dim, batch], y [out_dim, batch]. */
+size_t clb_difflogic_workspace_bytes(int64_t out_dim, int64_t K, int64_t batch, int dtype);
+int clb_difflogic_forward(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
+                          const int64_t* b, const void* w, const uint8_t* gate_seq, int64_t out_dim, int64_t K,
+                          void* y, void* workspace, size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces difflogic_cuda.backward_w(x, a, b, gate_seq, grad_y) -> grad_w (d loss / d prob)
+ * (compactlogic/cuda/difflogic.cpp:67-71, difflogic_kernel.cu:239-282).  grad_w [out_dim, K]. */
+int clb_difflogic_backward_w(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
+                             const int64_t* b, const uint8_t* gate_seq, const void* grad_y, int64_t out_dim,
+                             int64_t K, void* grad_w, void* workspace, size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces difflogic_cuda.backward_x(x, a, b, w, gate_seq, grad_y, starts, ys, gate_codes) -> grad_x
+ * (compactlogic/cuda/difflogic.cpp:72-77, difflogic_kernel.cu:285-333): a deterministic gather over
+ * the inverse connection index built by LogicLayer.refresh_backward_index (compactlogic.py:184-274).
+ * starts int64 [in_dim+1], ys int64 [2*out_dim*K], gate_codes int8 [2*out_dim*K]. */
+int clb_difflogic_backward_x(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
+                             const int64_t* b, const void* w, const uint8_t* gate_seq, const void* grad_y,
+                             const int64_t* starts, const int64_t* ys, const int8_t* gate_codes, int64_t out_dim,
+                             int64_t K, void* grad_x, void* workspace, size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces difflogic_cuda.backward_x_atomicAdd(x, a, b, w, gate_seq, grad_y) -> grad_x
+ * (compactlogic/cuda/difflogic.cpp:99-104, difflogic_kernel.cu:613-656): scatter formulation.
+ * Unlike the reference it does not synchronise the device. */
+int clb_difflogic_backward_x_atomic(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
+                                    const int64_t* b, const void* w, const uint8_t* gate_seq, const void* grad_y,
+                                    int64_t out_dim, int64_t K, void* grad_x, void* workspace,
+                                    size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces difflogic_cuda.eval(x, a, b, w_u8, gate_seq) -> y (compactlogic/cuda/difflogic.cpp:78-83,
+ * difflogic_kernel.cu:341-411): the argmax gate's real polynomial, w_u8 [out_dim] selects the slot. */
+int clb_difflogic_eval(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
+                       const int64_t* b, const uint8_t* w_sel, const uint8_t* gate_seq, int64_t out_dim, int64_t K,
+                       void* y, void* workspace, size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces difflogic_cuda.tensor_packbits_cuda(t, bit_count) -> (words, pad_len)
+ * (compactlogic/cuda/difflogic.cpp:84-89, difflogic_kernel.cu:453-494).  t bool/uint8 [rows, cols];
+ * out [rows, ceil(cols/bit_count)] words of bit_count in {8,16,32,64} (bit i of word c = column
+ * c*bit_count+i).  *pad_len_host receives (bit_count - cols % bit_count) % bit_count. */
+int clb_tensor_packbits(const uint8_t* t, int64_t rows, int64_t cols, int bit_count, void* out,
+                        int64_t* pad_len_host, clb_stream_t stream);
+
+/* Replaces difflogic_cuda.groupbitsum(words, pad_len, k) -> counts [batch, k] int32
+ * (compactlogic/cuda/difflogic.cpp:90-98, difflogic_kernel.cu:535-568), batch = nwords*bits - pad_len.
+ * Returns CLB_ERR_DIVISIBILITY when rows % k != 0 (the reference raises ValueError). */
+int clb_groupbitsum(const void* words, int64_t rows, int64_t nwords, int bit_count, int64_t pad_len, int64_t k,
+                    int32_t* counts, clb_stream_t stream);
+
+/* Conv layer, NCHW activations.  offsets_ch int32, offsets_h/offsets_w int8, all [2, c_out, K]
+ * (compactlogic.py:642-698); stride/pad/ks as passed by ConvLayerCudaFunction (compactlogic.py:847-867).
+ * h_out = (h_in + 2 pad - ks) / stride + 1 (convlogic_kernel.cu:159-160). */
+size_t clb_convlogic_workspace_bytes(int64_t n, int64_t c_in, int64_t h_in, int64_t w_in, int64_t c_out,
+                                     int64_t h_out, int64_t w_out, int64_t K, int dtype);
+
+/* Replaces convlogic_cuda.forward(x, och, oh, ow, w, gate_seq, stride, pad, ks) -> y
+ * (compactlogic/cuda/convlogic.cpp:50-60, convlogic_kernel.cu:140-188). */
+int clb_convlogic_forward(int dtype, const void* x, int64_t n, int64_t c_in, int64_t h_in, int64_t w_in,
+                          const int32_t* offsets_ch, const int8_t* offsets_h, const int8_t* offsets_w,
+                          const void* w, const uint8_t* gate_seq, int64_t c_out, int64_t K, int stride, int pad,
+                          int ks, void* y, void* workspace, size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces convlogic_cuda.backward_x(x, och, oh, ow, w, gate_seq, grad_y, stride, pad) -> grad_x
+ * (compactlogic/cuda/convlogic.cpp:61-75, convlogic_kernel.cu:248-293).  h_out/w_out come from grad_y. */
+int clb_convlogic_backward_x(int dtype, const void* x, int64_t n, int64_t c_in, int64_t h_in, int64_t w_in,
+                             const int32_t* offsets_ch, const int8_t* offsets_h, const int8_t* offsets_w,
+                             const void* w, const uint8_t* gate_seq, const void* grad_y, int64_t c_out,
+                             int64_t h_out, int64_t w_out, int64_t K, int stride, int pad, void* grad_x,
+                             void* workspace, size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces convlogic_cuda.backward_w(x, och, oh, ow, gate_seq, grad_y, stride) -> grad_w
+ * (compactlogic/cuda/convlogic.cpp:76-89, convlogic_kernel.cu:385-430). */
+int clb_convlogic_backward_w(int dtype, const void* x, int64_t n, int64_t c_in, int64_t h_in, int64_t w_in,
+                             const int32_t* offsets_ch, const int8_t* offsets_h, const int8_t* offsets_w,
+                             const uint8_t* gate_seq, const void* grad_y, int64_t c_out, int64_t h_out,
+                             int64_t w_out, int64_t K, int stride, void* grad_w, void* workspace,
+                             size_t workspace_bytes, clb_stream_t stream);
+
+/* Replaces convlogic_cuda.eval(x, och, oh, ow, w_u8, gate_seq, stride, pad, ks) -> y
+ * (compactlogic/cuda/convlogic.cpp:90-104, convlogic_kernel.cu:479-530). */
+int clb_convlogic_eval(int dtype, const void* x, int64_t n, int64_t c_in, int64_t h_in, int64_t w_in,
+                       const int32_t* offsets_ch, const int8_t* offsets_h, const int8_t* offsets_w,
+                       const uint8_t* w_sel, const uint8_t* gate_seq, int64_t c_out, int64_t K, int stride, int pad,
+                       int ks, void* y, void* workspace, size_t workspace_bytes, clb_stream_t stream);
+
+/* ===================================== 2. native fast path =====================================
+ * A layer is a slot table: slots int32 [n_out, K, 2] holds the input feature ids (a, b) of every
+ * candidate gate of every output neuron, -1 meaning the constant 0 (conv zero padding).  Weights and
+ * gates are per parameter row r = j / group: [n_out/group, K] (dense: group 1; conv: group =
+ * h_out*w_out).  Weights are in the arithmetic type (fp32, or fp64 for fp64 activations).
+ */
+
+/* Slot table of a dense LogicLayer from its int64 `indices` halves (compactlogic.py:160-182).
+ * err: optional device int32, OR-ed with 1 when an index is out of [0, in_dim); such slots read 0. */
+int clb_slots_dense(const int64_t* a, const int64_t* b, int64_t n_out, int64_t K, int64_t in_dim, int32_t* slots,
+                    int32_t* err, clb_stream_t stream);
+
+/* Slot table of a ConvLayer (compactlogic.py:642-698, offsets already shifted by -padding).
+ * Neuron j = (c * h_out + oy) * w_out + ox; input feature = (ch * h_in + y) * w_in + x. */
+int clb_slots_conv(const int32_t* offsets_ch, const int8_t* offsets_h, const int8_t* offsets_w, int64_t c_out,
+                   int64_t K, int64_t c_in, int64_t h_in, int64_t w_in, int64_t h_out, int64_t w_out, int stride,
+                   int32_t* slots, int32_t* err, clb_stream_t stream);
+
+/* Forward of one layer over columns [0, ncols) (LogicLayer.forward_cuda + LogicLayerCudaFunction.forward,
+ * compactlogic.py:83-118,483-486; eval with mode CLB_W_SELECT, compactlogic.py:120-130).
+ * If gs_acc != NULL the layer's GroupSum (compactlogic.py:450-468) is fused: y is not written and
+ * gs_acc [gs_k, ld_gs] (arithmetic type, pre-zeroed) accumulates sum over the neurons of each class,
+ * class(j) = j / gs_size. */
+int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots, int64_t n_out,
+                      int64_t K, int64_t group, int weight_mode, const void* weights, const uint8_t* gates,
+                      const uint8_t* select, int has_pad, void* y, int64_t ldy, void* gs_acc, int64_t gs_k,
+                      int64_t gs_size, int64_t ld_gs, clb_stream_t stream);
+
+/* Number of column chunks of the backward pass = rows of the partials scratch [nchunks, n_out, K]. */
+int64_t clb_logic_backward_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, const void* grad_y,
+                                  int64_t ldgy, const void* gs_grad, int64_t ld_gs, const void* grad_x, int64_t ldgx);
+
+/* Fused backward of one layer (LogicLayerCudaFunction.backward, compactlogic.py:488-508):
+ *  - grad_x (optional, [in, ldgx] arithmetic type): activation gradient; zeroed first when zero_grad_x.
+ *  - partials (optional, [nchunks, n_out, K]): per-chunk d loss / d prob, folded by
+ *    clb_logic_grad_finalize.  partials_chunks must equal clb_logic_backward_chunks() for the same
+ *    pointers and strides (the column split depends on their 16-byte alignment).
+ * grad_y [n_out, ldgy] arithmetic type; or, with gs_grad != NULL, the fused GroupSum's backward:
+ * grad_y[j, n] = gs_grad[class(j), n] * gs_scale. */
+int clb_logic_backward(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots, int64_t n_out,
+                       int64_t K, int64_t group, int weight_mode, const void* weights, const uint8_t* gates,
+                       int has_pad, const void* grad_y, int64_t ldgy, const void* gs_grad, int64_t gs_k,
+                       int64_t gs_size, int64_t ld_gs, double gs_scale, void* grad_x, int64_t ldgx, int zero_grad_x,
+                       int64_t in_features, void* partials, int64_t partials_chunks, clb_stream_t stream);
+
+/* partials -> per-row gradient [n_out/group, K] in the arithmetic type: w.r.t. the logits (softmax
+ * backward fused) for CLB_W_LOGITS, w.r.t. the probabilities for CLB_W_PROBS. */
+int clb_logic_grad_finalize(int dtype, const void* partials, int64_t nchunks, int64_t n_out, int64_t K,
+                            int64_t group, int weight_mode, const void* weights, void* grad_w, clb_stream_t stream);
+
+/* Layout helpers: dst[c, r] = src[r, c] for elem_bytes in {1,2,4,8}; fp32 <-> bf16 casts. */
+int clb_transpose(int elem_bytes, const void* src, int64_t rows, int64_t cols, int64_t ld_src, void* dst,
+                  int64_t ld_dst, clb_stream_t stream);
+int clb_cast(int src_dtype, const void* src, int dst_dtype, void* dst, int64_t n, clb_stream_t stream);
+
+/* ---- bit-packed discrete inference (uint64 words, bit i of word w = sample 64 w + i) ---- */
+
+/* x [batch, features] sample-major with values in {0,1} (bit = x > 0.5) -> out [features, ldw]. */
+int clb_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, uint64_t* out,
+                    int64_t ldw, clb_stream_t stream);
+
+/* Frozen layer tables: sel_ab int32 [n_out, 2], sel_gate uint8 [n_out] from the slot table and the
+ * per-row chosen slot (the `w` buffer of a frozen layer, or argmax of the logits; compactlogic.py:120-130). */
+int clb_packed_select(const int32_t* slots, const uint8_t* gates, const uint8_t* select, int64_t n_out, int64_t K,
+                      int64_t group, int32_t* sel_ab, uint8_t* sel_gate, clb_stream_t stream);
+
+/* One packed layer over word columns [0, nwords): y[j, w] = gate_j(x[a_j, w], x[b_j, w]). */
+int clb_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab, const uint8_t* sel_gate,
+                     int64_t n_out, uint64_t* y, int64_t ldy, clb_stream_t stream);
+
+/* Last packed layer fused with GroupSum: counts[(sample0 + n) * k + class] += number of neurons of the
+ * class whose output bit for sample n is 1 (n < nsamples; class(j) = j / class_size).  counts int32
+ * [*, k], accumulated (zero it first). */
+int clb_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
+                           const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size, int32_t* counts,
+                           int64_t sample0, int64_t nsamples, clb_stream_t stream);
+
+/* Packed GroupSum over stored words [rows, nwords] uint64: same accumulation as above. */
+int clb_packed_count(const uint64_t* words, int64_t rows, int64_t nwords, int64_t k, int64_t class_size,
+                     int32_t* counts, int64_t sample0, int64_t nsamples, clb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COMPACTLOGIC_B200_H */

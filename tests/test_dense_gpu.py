@@ -1,0 +1,163 @@
+"""Dense soft / eval logic layer on the GPU against the CPU oracle (and the reference API shims)."""
+import numpy as np
+import pytest
+import torch
+
+import compactlogic_b200 as cl
+from compactlogic_b200 import _lib as L
+from compactlogic_b200 import difflogic_cuda
+from compactlogic_b200.functional import LayerSpec, LogicGroupSumFn, LogicLayerFn, eval_forward
+from oracle import oracle as O
+
+from helpers import RTOL, assert_close, cuda, rand_dense
+
+pytestmark = pytest.mark.gpu
+
+
+def _spec(a, b, g, in_dim):
+    out, K = a.shape
+    idx = cuda(np.stack([a, b]).astype(np.int64))
+    slots = torch.empty(out, K, 2, dtype=torch.int32, device="cuda")
+    L.call("clb_slots_dense", L.ptr(idx[0]), L.ptr(idx[1]), out, K, in_dim, L.ptr(slots), 0, L.stream())
+    return LayerSpec(slots, cuda(g), out, K, 1, in_dim, False)
+
+
+SHAPES = [(16, 24, 16, 1), (40, 30, 16, 3), (64, 64, 4, 64), (100, 80, 7, 130), (784, 512, 16, 256),
+          (33, 20, 1, 8), (50, 64, 8, 96), (20, 12, 32, 40)]
+
+
+@pytest.mark.parametrize("in_dim,out,K,B", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_forward_backward_vs_oracle(in_dim, out, K, B, dtype):
+    x, a, b, logits, g, gy = rand_dense(in_dim * 7 + K, in_dim, out, K, B)
+    spec = _spec(a, b, g, in_dim)
+    xt = cuda(x, dtype).requires_grad_(True)
+    w = cuda(logits, dtype).requires_grad_(True)
+    y = LogicLayerFn.apply(xt, w, spec)
+    p = O.softmax(logits)
+    assert_close(y, O.dense_forward(x, a, b, p, g), RTOL[dtype], "y")
+    y.backward(cuda(gy, dtype))
+    assert_close(xt.grad, O.dense_backward_x(x, a, b, p, g, gy), RTOL[dtype], "grad_x")
+    assert_close(w.grad, O.softmax_backward(p, O.dense_backward_w(x, a, b, g, gy)), RTOL[dtype], "grad_logits")
+
+
+@pytest.mark.parametrize("in_dim,out,K,B,k", [(50, 40, 16, 64, 10), (30, 33, 4, 7, 4), (784, 1000, 16, 256, 10)])
+def test_groupsum_fused_vs_oracle(in_dim, out, K, B, k):
+    x, a, b, logits, g, _ = rand_dense(in_dim + out, in_dim, out, K, B)
+    spec = _spec(a, b, g, in_dim)
+    xt = cuda(x, torch.float32).requires_grad_(True)
+    w = cuda(logits, torch.float32).requires_grad_(True)
+    size = -(-out // k)
+    acc = LogicGroupSumFn.apply(xt, w, spec, k, size)
+    p = O.softmax(logits)
+    y = O.dense_forward(x, a, b, p, g)
+    assert_close(acc.t() / 2.0, O.group_sum(y.T, k, 2.0), 1e-5, "logits")
+    gl = np.random.default_rng(0).standard_normal((B, k))
+    (acc.t() / 2.0).backward(cuda(gl, torch.float32))
+    gy = O.group_sum_backward(gl, out, k, 2.0).T
+    assert_close(xt.grad, O.dense_backward_x(x, a, b, p, g, gy), 1e-5, "grad_x")
+    assert_close(w.grad, O.softmax_backward(p, O.dense_backward_w(x, a, b, g, gy)), 1e-5, "grad_logits")
+
+
+@pytest.mark.parametrize("B", [1, 5, 64, 200])
+def test_eval_select_bitexact(B):
+    x, a, b, logits, g, _ = rand_dense(B, 60, 70, 16, B, binary_input=True)
+    spec = _spec(a, b, g, 60)
+    sel = O.argmax_first(logits)
+    y = eval_forward(cuda(x, torch.float32), spec, cuda(sel))
+    np.testing.assert_array_equal(y.cpu().numpy(), O.dense_eval(x, a, b, sel, g))
+
+
+def test_bf16_activations():
+    x, a, b, logits, g, gy = rand_dense(5, 256, 300, 4, 512)
+    spec = _spec(a, b, g, 256)
+    xb = cuda(x, torch.bfloat16)
+    xr = xb.double().cpu().numpy()  # the oracle sees the bf16-rounded inputs
+    xt = xb.clone().requires_grad_(True)
+    w = cuda(logits, torch.float32).requires_grad_(True)
+    y = LogicLayerFn.apply(xt, w, spec)
+    p = O.softmax(logits)
+    assert_close(y, O.dense_forward(xr, a, b, p, g), 1e-2, "y bf16")
+    y.backward(cuda(gy, torch.bfloat16))
+    gyr = cuda(gy, torch.bfloat16).double().cpu().numpy()
+    assert_close(w.grad, O.softmax_backward(p, O.dense_backward_w(xr, a, b, g, gyr)), 1e-2, "grad_logits bf16")
+
+
+def test_gradcheck_float64():
+    x, a, b, logits, g, _ = rand_dense(9, 7, 6, 3, 4)
+    spec = _spec(a, b, g, 7)
+    xt = cuda(x, torch.float64).requires_grad_(True)
+    w = cuda(logits, torch.float64).requires_grad_(True)
+    assert torch.autograd.gradcheck(lambda xx, ww: LogicLayerFn.apply(xx, ww, spec), (xt, w), eps=1e-6, atol=1e-8)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_reference_api_shims(dtype):
+    in_dim, out, K, B = 70, 90, 16, 48
+    x, a, b, logits, g, gy = rand_dense(3, in_dim, out, K, B)
+    p = O.softmax(logits)
+    xt, at, bt, pt, gt, gyt = cuda(x, dtype), cuda(a), cuda(b), cuda(p, dtype), cuda(g), cuda(gy, dtype)
+    assert_close(difflogic_cuda.forward(xt, at, bt, pt, gt), O.dense_forward(x, a, b, p, g), RTOL[dtype], "forward")
+    assert_close(difflogic_cuda.backward_w(xt, at, bt, gt, gyt), O.dense_backward_w(x, a, b, g, gy), RTOL[dtype],
+                 "backward_w")
+    starts, ys, codes = O.inverse_index(a, b, in_dim)
+    gx_ref = O.dense_backward_x(x, a, b, p, g, gy)
+    gx = difflogic_cuda.backward_x(xt, at, bt, pt, gt, gyt, cuda(starts), cuda(ys), cuda(codes))
+    assert_close(gx, gx_ref, RTOL[dtype], "backward_x")
+    assert_close(difflogic_cuda.backward_x_atomicAdd(xt, at, bt, pt, gt, gyt), gx_ref, RTOL[dtype], "backward_x_atomic")
+    sel = O.argmax_first(logits)
+    xb = (x > 0.5).astype(np.float64)
+    np.testing.assert_array_equal(difflogic_cuda.eval(cuda(xb, dtype), at, bt, cuda(sel), gt).cpu().numpy(),
+                                  O.dense_eval(xb, a, b, sel, g))
+
+
+def test_shim_input_checks():
+    x = torch.rand(4, 3)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        difflogic_cuda.forward(x, x, x, x, x)
+    xt = torch.rand(3, 4, device="cuda").t()
+    with pytest.raises(RuntimeError, match="contiguous"):
+        difflogic_cuda.forward(xt, xt, xt, xt, xt)
+
+
+def test_layer_module_matches_reference_math():
+    """LogicLayer module (train mode, then eval) on the GPU vs the oracle restatement of the reference
+    LogicLayer.forward_cuda / forward_cuda_eval (compactlogic.py:74-130)."""
+    torch.manual_seed(0)
+    layer = cl.LogicLayer(96, 120, num_gates=16)
+    idx = layer.indices.numpy()
+    g = layer.gate_sequence.numpy()
+    logits = layer.weights.detach().numpy().astype(np.float64)
+    layer = layer.cuda()
+    x = (np.random.default_rng(1).random((40, 96)) < 0.5).astype(np.float32)
+    xt = cuda(x).requires_grad_(True)
+    y = layer(xt)
+    p = O.softmax(logits)
+    y_ref = O.dense_forward(x.T, idx[0], idx[1], p, g).T
+    assert_close(y, y_ref, 1e-5, "module y")
+    gy = np.random.default_rng(2).standard_normal(y_ref.shape)
+    y.backward(cuda(gy, torch.float32))
+    assert_close(layer.weights.grad, O.softmax_backward(p, O.dense_backward_w(x.T, idx[0], idx[1], g, gy.T)), 1e-5,
+                 "module grad")
+    assert_close(xt.grad, O.dense_backward_x(x.T, idx[0], idx[1], p, g, gy.T).T, 1e-5, "module grad_x")
+    layer.eval()
+    ye = layer(cuda(x))
+    np.testing.assert_array_equal(ye.cpu().numpy(), O.dense_eval(x.T, idx[0], idx[1], O.argmax_first(logits), g).T)
+    # indices changed in place -> slot table rebuilt
+    with torch.no_grad():
+        layer.indices[0, :, :] = 0
+    ye2 = layer(cuda(x))
+    idx2 = layer.indices.cpu().numpy()
+    np.testing.assert_array_equal(ye2.cpu().numpy(),
+                                  O.dense_eval(x.T, idx2[0], idx2[1], O.argmax_first(logits), g).T)
+
+
+def test_frozen_layer_runs_eval_in_train_mode():
+    torch.manual_seed(4)
+    layer = cl.LogicLayer(30, 40, num_gates=8).cuda()
+    layer.freeze()
+    layer.train()
+    x = (torch.rand(10, 30, device="cuda") < 0.5).float()
+    idx = layer.indices.cpu().numpy()
+    ref = O.dense_eval(x.cpu().numpy().T, idx[0], idx[1], layer.w.cpu().numpy(), layer.gate_sequence.cpu().numpy()).T
+    np.testing.assert_array_equal(layer(x).cpu().numpy(), ref)
