@@ -73,7 +73,7 @@ class LogicLayer(torch.nn.Module):
     def _to_feature_major(self, x):
         assert x.ndim == 2, x.ndim
         xt = x.transpose(0, 1)
-        if xt.stride(1) != 1 or xt.stride(0) != xt.shape[1]:
+        if xt.shape[1] > 1 and (xt.stride(1) != 1 or xt.stride(0) < xt.shape[1]):
             xt = xt.contiguous()
         assert xt.shape[0] == self.in_dim, (xt.shape, self.in_dim)
         return xt

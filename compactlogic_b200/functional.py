@@ -25,9 +25,53 @@ class LayerSpec:
     has_pad: bool
 
 
+class KernelTimer:
+    """Optional per-launch CUDA-event timing of the layer kernels (used by bench.py for the roofline).
+
+    While enabled, every forward / backward kernel launch is bracketed by events on the launching
+    stream and recorded with its algorithmic (compulsory) byte count:
+      forward  = e*B*(in + out) + n_out*K*8 + rows*K*5        (y not written when GroupSum is fused)
+      backward = e*B*in + a*B*out + a*B*in + n_out*K*8 + rows*K*5
+                 (gy term dropped when synthesised from the fused GroupSum, gx term when not needed)
+    with e the activation element size, a the gradient element size, slots int32 pairs, gate ids
+    uint8 and logits fp32."""
+
+    def __init__(self):
+        self.enabled = False
+        self.records = []
+
+    def reset(self):
+        self.records = []
+
+    def launch(self, kind, nbytes, fn):
+        if not self.enabled:
+            return fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = fn()
+        e.record()
+        self.records.append((kind, s, e, nbytes))
+        return out
+
+    def summary(self):
+        """{kind: (launches, total_ms, total_bytes)} (call after a synchronize)."""
+        res = {}
+        for kind, s, e, nb in self.records:
+            n, ms, b = res.get(kind, (0, 0.0, 0))
+            res[kind] = (n + 1, ms + s.elapsed_time(e), b + nb)
+        return res
+
+
+TIMER = KernelTimer()
+
+
+def _param_bytes(spec: "LayerSpec") -> int:
+    return spec.n_out * spec.K * 8 + (spec.n_out // spec.group) * spec.K * 5
+
+
 def _check_x(xt: torch.Tensor, spec: LayerSpec) -> None:
     L.require_cuda(xt)
-    if xt.dim() != 2 or xt.shape[0] != spec.in_features or xt.stride(1) != 1:
+    if xt.dim() != 2 or xt.shape[0] != spec.in_features or (xt.shape[1] > 1 and xt.stride(1) != 1):
         raise RuntimeError(f"expected feature-major activations [{spec.in_features}, batch] with unit column stride, "
                            f"got shape {tuple(xt.shape)} strides {xt.stride()}")
 
@@ -37,10 +81,13 @@ def forward_into(xt: torch.Tensor, weights: Optional[torch.Tensor], spec: LayerS
                  gs_acc: Optional[torch.Tensor] = None, gs_size: int = 0) -> None:
     _check_x(xt, spec)
     B = xt.shape[1]
-    L.call("clb_logic_forward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
-           spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), L.ptr(select), int(spec.has_pad), L.ptr(y),
-           y.stride(0) if y is not None else 0, L.ptr(gs_acc), gs_acc.shape[0] if gs_acc is not None else 0, gs_size,
-           gs_acc.stride(0) if gs_acc is not None else 0, L.stream(xt.device))
+    e = xt.element_size()
+    nbytes = e * B * (spec.in_features + (spec.n_out if y is not None else 0)) + _param_bytes(spec)
+    TIMER.launch("forward" if mode != L.W_SELECT else "eval", nbytes, lambda: L.call(
+        "clb_logic_forward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
+        spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), L.ptr(select), int(spec.has_pad), L.ptr(y),
+        y.stride(0) if y is not None else 0, L.ptr(gs_acc), gs_acc.shape[0] if gs_acc is not None else 0, gs_size,
+        gs_acc.stride(0) if gs_acc is not None else 0, L.stream(xt.device)))
 
 
 def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode: int,
@@ -59,15 +106,20 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
         chunks = int(L.lib().clb_logic_backward_chunks(L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, gy_ptr,
                                                        ldgy, gs_ptr, ld_gs, L.ptr(gx), B))
         part = torch.empty(max(chunks, 1), spec.n_out, spec.K, dtype=acc, device=dev)
-    L.call("clb_logic_backward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
-           spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), int(spec.has_pad), gy_ptr, ldgy, gs_ptr, gs_k,
-           gs_size, ld_gs, float(gs_scale), L.ptr(gx), B, 1, spec.in_features, L.ptr(part), chunks,
-           L.stream(dev))
+    a = torch.empty((), dtype=acc).element_size()
+    nbytes = (xt.element_size() * B * spec.in_features + (a * B * spec.n_out if gy is not None else 0) +
+              (a * B * spec.in_features if need_gx else 0) + _param_bytes(spec))
+    TIMER.launch("backward", nbytes, lambda: L.call(
+        "clb_logic_backward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
+        spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), int(spec.has_pad), gy_ptr, ldgy, gs_ptr, gs_k,
+        gs_size, ld_gs, float(gs_scale), L.ptr(gx), B, 1, spec.in_features, L.ptr(part), chunks, L.stream(dev)))
     gw = None
     if need_gw:
         gw = torch.empty(spec.n_out // spec.group, spec.K, dtype=acc, device=dev)
-        L.call("clb_logic_grad_finalize", L.dtype_code(xt.dtype), L.ptr(part), chunks if B > 0 else 0, spec.n_out,
-               spec.K, spec.group, mode, L.ptr(weights), L.ptr(gw), L.stream(dev))
+        TIMER.launch("finalize", (max(chunks, 1) * spec.n_out + spec.n_out // spec.group) * spec.K * a,
+                     lambda: L.call("clb_logic_grad_finalize", L.dtype_code(xt.dtype), L.ptr(part),
+                                    chunks if B > 0 else 0, spec.n_out, spec.K, spec.group, mode, L.ptr(weights),
+                                    L.ptr(gw), L.stream(dev)))
     return gx, gw
 
 

@@ -38,7 +38,9 @@ class PackedLogicNet:
             raise ValueError("PackedLogicNet needs a model ending in GroupSum")
         gs = mods[-1]
         self.k, self.tau = int(gs.k), float(gs.tau)
-        self.device = torch.device(device) if device is not None else mods[0].weights.device
+        first = next((m for m in mods if isinstance(m, LogicLayer)), None)
+        self.device = torch.device(device) if device is not None else (first.weights.device if first is not None else
+                                                                       torch.device('cuda'))
         self.chunk_words = int(chunk_words)
         self.layers: List[_Frozen] = []
         for m in mods[:-1]:

@@ -1,0 +1,96 @@
+"""Multi-GPU execution of the logic-layer hot path (one process per GPU, torch.distributed).
+
+* Data-parallel training: parameters are replicated; each rank runs its slice of the batch and the
+  gate-logit gradients are summed with an NCCL all-reduce over NVLink.  One bucket per layer (the
+  layer's [rows, K] fp32 logit gradient), launched from a post-accumulate hook the moment that layer's
+  backward finishes, so the transfer overlaps the backward of the layers below it.  After the last
+  bucket the gradients are averaged; clipping and the optimizer then run identically on every rank
+  (the reference's single-GPU loop clips after backward, experiments/experiment_script.py:287).
+* Resampling and freezing consume RNG / read parameters: ``broadcast_layer_buffers`` makes rank 0's
+  connection buffers authoritative after such a host-side update.
+* Packed inference shards samples; ranks are independent until ``gather_counts`` collects the
+  per-rank [n_local, k] class counts.
+
+The reference has no distributed code; this module is new.
+"""
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+
+class GradAllReduce:
+    """Per-layer, overlapped all-reduce of the gradients of ``params``.
+
+    Usage per step: loss.backward(); sync.finish(); clip; optimizer.step().
+    """
+
+    def __init__(self, params, group=None, average: bool = True):
+        self.params: List[torch.nn.Parameter] = [p for p in params if p.requires_grad]
+        self.group = group
+        self.average = average
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self._works = []
+        self._handles = []
+        if self.world > 1:
+            for p in self.params:
+                self._handles.append(p.register_post_accumulate_grad_hook(self._hook))
+
+    def _hook(self, p):
+        if p.grad is None:
+            return
+        self._works.append((p, dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True)))
+
+    def finish(self):
+        """Wait for all buckets of this step and average them."""
+        works, self._works = self._works, []
+        for p, w in works:
+            w.wait()
+            if self.average:
+                p.grad.div_(self.world)
+
+    def remove(self):
+        for h in self._handles:
+            h.remove()
+        self._handles = []
+
+
+def broadcast_layer_buffers(model: torch.nn.Module, src: int = 0, group=None) -> None:
+    """Make every rank's parameters and buffers equal to rank `src`'s (after resampling/freezing)."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return
+    with torch.no_grad():
+        for t in list(model.parameters()) + list(model.buffers()):
+            dist.broadcast(t.data, src=src, group=group)
+
+
+def shard_range(n: int, rank: int, world: int, align: int = 64):
+    """Contiguous [lo, hi) slice of n samples for `rank`, boundaries on multiples of `align` (whole
+    packed words) except the last."""
+    units = -(-n // align)
+    lo_u = units * rank // world
+    hi_u = units * (rank + 1) // world
+    return min(n, lo_u * align), min(n, hi_u * align)
+
+
+def gather_counts(local_counts: torch.Tensor, n_total: int, group=None) -> torch.Tensor:
+    """All-gather the per-rank [n_local, k] class counts into [n_total, k] on every rank."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return local_counts
+    world = dist.get_world_size(group)
+    k = local_counts.shape[1]
+    sizes = [shard_range(n_total, r, world) for r in range(world)]
+    cap = max(hi - lo for lo, hi in sizes)
+    buf = torch.zeros(cap, k, dtype=local_counts.dtype, device=local_counts.device)
+    buf[:local_counts.shape[0]] = local_counts
+    out = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(out, buf, group=group)
+    return torch.cat([o[:hi - lo] for o, (lo, hi) in zip(out, sizes)], 0)
+
+
+def max_over_ranks(value: float, device: Optional[torch.device] = None, group=None) -> float:
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return float(t.item())

@@ -58,7 +58,7 @@ def test_packed_net_matches_reference_circuit(golden, chunk_words):
     np.testing.assert_array_equal(torch.round(model(x) * float(d["tau"])).to(torch.int32).cpu().numpy(), d["counts"])
 
 
-@pytest.mark.parametrize("B,widths,k", [(1, [50, 40, 33], 4), (65, [100, 64, 64, 10], 10), (1000, [200, 300, 300, 55], 7),
+@pytest.mark.parametrize("B,widths,k", [(1, [50, 40, 33], 4), (65, [100, 64, 64, 40], 10), (1000, [200, 300, 300, 150], 7),
                                         (4096, [784, 2000, 2000, 1000], 10)])
 def test_packed_net_vs_oracle(B, widths, k):
     torch.manual_seed(B)
