@@ -28,6 +28,7 @@ _SIGS = {
     "clb_difflogic_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
     "clb_difflogic_forward": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _sz, _p]),
     "clb_difflogic_backward_w": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _sz, _p]),
+    "clb_difflogic_backward_w_noalloc": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p]),
     "clb_difflogic_backward_x": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                                         _sz, _p]),
     "clb_difflogic_backward_x_atomic": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _sz,

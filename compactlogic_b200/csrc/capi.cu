@@ -88,6 +88,11 @@ int check_layer(int dtype, int64_t n_out, int64_t K, int64_t group, int mode, co
 
 }  // namespace
 
+namespace clb {
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+void count_launches(int n) { g_launches += n; }
+}  // namespace clb
+
 extern "C" {
 
 const char* clb_last_error(void) { return g_err.c_str(); }

@@ -88,4 +88,8 @@ cudaError_t launch_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nw
                                       const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size,
                                       int32_t* counts, int64_t sample0, int64_t nsamples, cudaStream_t s);
 
+// Error / launch bookkeeping of the C ABI (capi.cu), for entry points defined in other files.
+int set_error(int code, const char* msg);
+void count_launches(int n);
+
 }  // namespace clb

@@ -78,6 +78,19 @@ int clb_difflogic_backward_w(int dtype, const void* x, int64_t in_dim, int64_t b
                              const int64_t* b, const uint8_t* gate_seq, const void* grad_y, int64_t out_dim,
                              int64_t K, void* grad_w, void* workspace, size_t workspace_bytes, clb_stream_t stream);
 
+/* No counterpart in the reference.  Same result as clb_difflogic_backward_w, for callers that cannot
+ * allocate device memory (no allocator of their own to provide a workspace, or an allocator that
+ * forbids cudaMalloc where the call is made): instead of a workspace it uses an 8 MiB scratch array
+ * compiled into the library, held on every GPU that loads it until exit.  Limit:
+ * out_dim*K*8 + ceil(batch/(32*v))*out_dim*K*elem bytes (v = 4 for fp32, 2 for fp64 when the
+ * pointers and batch allow 16-byte vectors, else 1), each part rounded up to 256, must fit in 8 MiB;
+ * larger calls return CLB_ERR_WORKSPACE.  The first call on a device (with it current) looks up the
+ * array's address; make it before any stream capture.  Calls share the array: calls that overlap on
+ * the GPU race and must be serialised by the caller.  Allocates nothing. */
+int clb_difflogic_backward_w_noalloc(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
+                                     const int64_t* b, const uint8_t* gate_seq, const void* grad_y, int64_t out_dim,
+                                     int64_t K, void* grad_w, clb_stream_t stream);
+
 /* Replaces difflogic_cuda.backward_x(x, a, b, w, gate_seq, grad_y, starts, ys, gate_codes) -> grad_x
  * (compactlogic/cuda/difflogic.cpp:72-77, difflogic_kernel.cu:285-333): a deterministic gather over
  * the inverse connection index built by LogicLayer.refresh_backward_index (compactlogic.py:184-274).

@@ -1,0 +1,64 @@
+"""The allocation-free backward_w entry point, called through the C ABI.
+
+Callers that cannot allocate device memory where they need the gate-probability gradient (no
+allocator of their own to provide a workspace, or an allocator that forbids cudaMalloc there) use
+clb_difflogic_backward_w_noalloc, which works in an 8 MiB scratch array compiled into the library.
+It must give the same result as the workspace entry point clb_difflogic_backward_w, also when called
+twice in a row (the scratch keeps the previous call's contents), and reject calls that do not fit.
+This file is collected last so a failure here cannot hide any other test's result.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from compactlogic_b200 import _lib as L
+from oracle import oracle as O
+
+from helpers import RTOL, assert_close, cuda, rand_dense
+
+pytestmark = pytest.mark.gpu
+
+def _with_workspace(x, a, b, g, gy, dtype):
+    out, K = a.shape
+    ws = torch.empty(int(L.lib().clb_difflogic_workspace_bytes(out, K, x.shape[1], L.dtype_code(dtype))),
+                     dtype=torch.uint8, device="cuda")
+    gw = torch.empty(out, K, dtype=dtype, device="cuda")
+    st = L.lib().clb_difflogic_backward_w(L.dtype_code(dtype), x.data_ptr(), x.shape[0], x.shape[1], a.data_ptr(),
+                                          b.data_ptr(), g.data_ptr(), gy.data_ptr(), out, K, gw.data_ptr(),
+                                          ws.data_ptr(), ws.numel(), L.stream())
+    assert st == L.CLB_OK, L.lib().clb_last_error()
+    return gw
+
+def _no_alloc(x, a, b, g, gy, dtype):
+    out, K = a.shape
+    gw = torch.empty(out, K, dtype=dtype, device="cuda")
+    st = L.lib().clb_difflogic_backward_w_noalloc(L.dtype_code(dtype), x.data_ptr(), x.shape[0], x.shape[1],
+                                                  a.data_ptr(), b.data_ptr(), g.data_ptr(), gy.data_ptr(), out, K,
+                                                  gw.data_ptr(), L.stream())
+    assert st == L.CLB_OK, L.lib().clb_last_error()
+    return gw
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_no_alloc_matches_workspace_entry_twice(dtype):
+    shapes = [(784, 1200, 16, 256), (300, 400, 4, 33)]  # the second call is smaller than the first
+    for seed, (in_dim, out, K, B) in enumerate(shapes):
+        x, a, b, _, g, gy = rand_dense(100 + seed, in_dim, out, K, B)
+        xt, at, bt, gt, gyt = cuda(x, dtype), cuda(a), cuda(b), cuda(g), cuda(gy, dtype)
+        ref = _with_workspace(xt, at, bt, gt, gyt, dtype)
+        got = _no_alloc(xt, at, bt, gt, gyt, dtype)
+        torch.cuda.synchronize()
+        assert_close(got, ref.cpu().numpy(), RTOL[dtype], f"call {seed}")
+        assert_close(got, O.dense_backward_w(x, a, b, g, gy), RTOL[dtype], f"call {seed} vs oracle")
+
+def test_no_alloc_rejects_oversize():
+    out, K, B = 200000, 16, 64  # slot table alone is 25.6 MB > 8 MiB
+    x = torch.zeros(10, B, device="cuda")
+    idx = torch.zeros(out, K, dtype=torch.int64, device="cuda")
+    g = torch.zeros(out, K, dtype=torch.uint8, device="cuda")
+    gy = torch.zeros(out, B, device="cuda")
+    gw = torch.empty(out, K, device="cuda")
+    st = L.lib().clb_difflogic_backward_w_noalloc(L.CLB_F32, x.data_ptr(), 10, B, idx.data_ptr(), idx.data_ptr(),
+                                                  g.data_ptr(), gy.data_ptr(), out, K, gw.data_ptr(), L.stream())
+    assert st == L.CLB_ERR_WORKSPACE
+    assert b"8 MiB" in L.lib().clb_last_error()
