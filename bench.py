@@ -204,8 +204,8 @@ def bench_c2(args, dev, rank, world):
         "metric": "train_samples_per_s", "value": round(world * B / (ms / 1e3), 1), "unit": "samples/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "c2: 784 -> 6x LogicLayer(64000, K=16) -> GroupSum(10, tau=10); CE, all-reduce, "
-                               "clip 10, Adam", "batch_per_gpu": B, "global_batch": B * world,
+        "config": {"workload": f"c2: 784 -> {C2['layers']}x LogicLayer(64000, K=16) -> GroupSum(10, tau=10); CE, "
+                               "all-reduce, clip 10, Adam", "batch_per_gpu": B, "global_batch": B * world,
                    "parallelism": f"dp{world}", "l2": "per-layer activations 262 MB > L2 126 MB (no flush)"},
         "step_hbm_bytes_algorithmic": step_bytes,
         "step_hbm_frac": round(step_bytes / (ms / 1e3) / 1e9 / hbm, 4),
@@ -287,18 +287,19 @@ def bench_c4(args, dev, rank, world, chunk_words):
     xw = torch.randint(-2**63, 2**63 - 1, (C4["in_dim"], W), dtype=torch.int64, device=dev, generator=g)
     counts = torch.zeros(n, C4["k"], dtype=torch.int32, device=dev)
     steps = max(1, args.steps // 2)
-    n0 = _lib.launches()
     with Clocks(dev.index) as clk:
         ms = timed(lambda: net.counts_packed(xw, n, counts), steps, max(1, args.warmup // 2), dev)
-    launches = (_lib.launches() - n0) * steps // (steps + max(1, args.warmup // 2))
+    launches = net.launches_per_pass * steps
     evals = C4["samples"] * C4["width"] * C4["layers"]
-    # end to end: packed words from pinned host memory in, counts back to pinned host memory
+    # end to end: packed words from pinned host memory into a fixed device buffer, counts back to
+    # pinned host memory
     xh = xw.cpu().pin_memory()
     ch = torch.empty_like(counts, device="cpu").pin_memory()
+    x_in = torch.empty_like(xw)
 
     def e2e():
-        x = xh.to(dev, non_blocking=True)
-        c = net.counts_packed(x, n, counts)
+        x_in.copy_(xh, non_blocking=True)
+        c = net.counts_packed(x_in, n, counts)
         ch.copy_(c, non_blocking=True)
 
     ms_e2e = timed(e2e, steps, 1, dev)
@@ -360,10 +361,13 @@ def main():
     ap.add_argument("--workload", default="c2", choices=["c2", "c4"])
     ap.add_argument("--no-packed", action="store_true", help="skip the packed-inference (c4) sub-measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    ap.add_argument("--chunk-words", type=int, default=32)
+    ap.add_argument("--chunk-words", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=None, help="override the c2 depth (profiling on a smaller case)")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work per baseline sample")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.layers:
+        C2["layers"] = args.layers
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -59,6 +59,15 @@ __device__ __forceinline__ Stage<A> carve(unsigned char* smem, int TN, int K, bo
     return s;
 }
 
+// Operands a gate does not depend on are marked -1, so neither the forward gather nor the backward
+// gather / scatter touches them: constant gates (0, 15) read nothing, gates A, B, not A, not B
+// (3, 5, 12, 10) read one operand.  Exact: the dropped terms have zero coefficients.
+__device__ __forceinline__ int2 used_operands(int2 s, const GatePoly& gp) {
+    if (gp.c1 == 0.f && gp.c3 == 0.f) s.x = -1;
+    if (gp.c2 == 0.f && gp.c3 == 0.f) s.y = -1;
+    return s;
+}
+
 __device__ __forceinline__ float exp_acc(float v) { return expf(v); }
 __device__ __forceinline__ double exp_acc(double v) { return exp(v); }
 
@@ -79,7 +88,7 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
                 const int k = a.select[r];
                 if (k < K) {
                     const GatePoly gp = gate_poly(g[k] & 15);
-                    st.ab[t * K] = slots[j * K + k];
+                    st.ab[t * K] = used_operands(slots[j * K + k], gp);
                     if (BACKWARD) {
                         st.cf[t * K] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
                         st.p[t * K] = (A)1;
@@ -101,7 +110,7 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
                 for (int k = 0; k < K; ++k) {
                     const A p = a.mode == CLB_W_LOGITS ? exp_acc(wr[k] - m) / sum : (w != nullptr ? wr[k] : (A)0);
                     const GatePoly gp = gate_poly(g[k] & 15);
-                    st.ab[t * K + k] = slots[j * K + k];
+                    st.ab[t * K + k] = used_operands(slots[j * K + k], gp);
                     if (BACKWARD) {
                         st.cf[t * K + k] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
                         st.p[t * K + k] = p;

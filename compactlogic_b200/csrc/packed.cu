@@ -174,8 +174,14 @@ __global__ void packed_select_kernel(const int2* __restrict__ slots, const uint8
         const int64_t r = j / group;
         const int k = select[r];
         if (k < K) {
-            sel_ab[j] = slots[j * K + k];
-            sel_gate[j] = gates[r * K + k] & 15;
+            // drop the operands the gate ignores (constant / single-input gates) so no load is issued
+            const int g = gates[r * K + k] & 15;
+            const GatePoly gp = gate_poly(g);
+            int2 s = slots[j * K + k];
+            if (gp.c1 == 0.f && gp.c3 == 0.f) s.x = -1;
+            if (gp.c2 == 0.f && gp.c3 == 0.f) s.y = -1;
+            sel_ab[j] = s;
+            sel_gate[j] = (uint8_t)g;
         } else {  // invalid selection: constant-0 gate
             sel_ab[j] = make_int2(-1, -1);
             sel_gate[j] = 0;
@@ -187,7 +193,9 @@ __device__ __forceinline__ uint64_t word_or_zero(const uint64_t* __restrict__ x,
     return idx >= 0 ? __ldg(x + (int64_t)idx * ldx + w) : 0ull;
 }
 
-// One packed layer.  TW lanes span word columns, 32/TW neurons per warp.
+// One packed layer.  TW lanes span word columns, 32/TW neurons per warp, and each thread handles
+// R neurons spaced 32/TW apart so that 2R independent 8-byte loads are in flight per thread.
+template <int R>
 __global__ void __launch_bounds__(256)
 packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
                     const uint8_t* __restrict__ sel_gate, int64_t n_out, uint64_t* __restrict__ y, int64_t ldy,
@@ -195,16 +203,30 @@ packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords,
     const int TW = 1 << tw_log2;
     const int lane = threadIdx.x & 31;
     const int64_t w = (int64_t)blockIdx.x * TW + (lane & (TW - 1));
-    const int64_t npw = 32 >> tw_log2;  // neurons per warp
+    const int64_t npw = 32 >> tw_log2;  // neurons per warp row
     const int64_t warp_global = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) >> 5;
-    const int64_t stride = ((int64_t)gridDim.y * blockDim.x >> 5) * npw;
+    const int64_t nwarps = ((int64_t)gridDim.y * blockDim.x) >> 5;
     if (w >= nwords) return;
-    for (int64_t j = warp_global * npw + (lane >> tw_log2); j < n_out; j += stride) {
-        const int2 ab = sel_ab[j];
-        const int g = sel_gate[j];
-        const uint64_t a = word_or_zero(x, ab.x, ldx, w);
-        const uint64_t b = word_or_zero(x, ab.y, ldx, w);
-        y[j * ldy + w] = gate_word<uint64_t>(g, a, b);
+    for (int64_t base = warp_global * npw * R; base < n_out; base += nwarps * npw * R) {
+        int2 ab[R];
+        int g[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t j = base + q * npw + (lane >> tw_log2);
+            ab[q] = j < n_out ? sel_ab[j] : make_int2(-1, -1);
+            g[q] = j < n_out ? sel_gate[j] : 0;
+        }
+        uint64_t va[R], vb[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            va[q] = word_or_zero(x, ab[q].x, ldx, w);
+            vb[q] = word_or_zero(x, ab[q].y, ldx, w);
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t j = base + q * npw + (lane >> tw_log2);
+            if (j < n_out) y[j * ldy + w] = gate_word<uint64_t>(g[q], va[q], vb[q]);
+        }
     }
 }
 
@@ -309,11 +331,12 @@ cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, 
     while ((1 << tw_log2) < nwords && tw_log2 < 5) ++tw_log2;
     const int64_t TW = 1 << tw_log2;
     const int64_t npw = 32 / TW;
-    const int64_t warps_needed = ceil_div64(n_out, npw);
+    constexpr int R = 4;
+    const int64_t warps_needed = ceil_div64(n_out, npw * R);
     const int64_t by = std::min<int64_t>(ceil_div64(warps_needed, 8), 65535);
     dim3 grid((unsigned)ceil_div64(nwords, TW), (unsigned)by);
-    packed_layer_kernel<<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate, n_out, y,
-                                             ldy, tw_log2);
+    packed_layer_kernel<R><<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate, n_out,
+                                                y, ldy, tw_log2);
     return cudaGetLastError();
 }
 

@@ -32,7 +32,7 @@ class PackedLogicNet:
     eval-mode output; predict(x) = argmax (first maximum, as torch.argmax).
     """
 
-    def __init__(self, model: torch.nn.Module, device=None, chunk_words: int = 32):
+    def __init__(self, model: torch.nn.Module, device=None, chunk_words: int = 16):
         mods = list(model)
         if not mods or not isinstance(mods[-1], GroupSum):
             raise ValueError("PackedLogicNet needs a model ending in GroupSum")
@@ -57,6 +57,9 @@ class PackedLogicNet:
         self.in_features = self.layers[0].in_features
         self.class_size = -(-self.layers[-1].n_out // self.k)
         self._bufs = None
+        self.use_graphs = True
+        self._graphs = {}
+        self.launches_per_pass = 0
 
     @torch.no_grad()
     def _freeze_tables(self, layer: LogicLayer) -> _Frozen:
@@ -93,20 +96,17 @@ class PackedLogicNet:
             self._bufs = tuple(torch.empty(rows, width, dtype=torch.int64, device=self.device) for _ in range(2))
         return self._bufs
 
-    @torch.no_grad()
-    def counts_packed(self, xw: torch.Tensor, batch: int, counts: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Class counts [batch, k] of pre-packed inputs xw [features, W]."""
+    def _run(self, xw: torch.Tensor, batch: int, counts: torch.Tensor) -> None:
+        """Enqueue one pass: per chunk, every layer then the fused last layer + class count."""
         W = xw.shape[1]
-        if counts is None:
-            counts = torch.zeros(batch, self.k, dtype=torch.int32, device=self.device)
-        else:
-            counts.zero_()
         cw = max(1, min(self.chunk_words, W))
         bufs = self._buffers(cw)
         s = L.stream(self.device)
+        counts.zero_()
+        n = 0
         for w0 in range(0, W, cw):
             nw = min(cw, W - w0)
-            src, ld_src = xw[:, w0:], W
+            src, ld_src = xw[:, w0:], xw.stride(0)
             for li, layer in enumerate(self.layers[:-1]):
                 dst = bufs[li % 2]
                 L.call("clb_packed_layer", L.ptr(src), ld_src, nw, L.ptr(layer.sel_ab), L.ptr(layer.sel_gate),
@@ -116,6 +116,39 @@ class PackedLogicNet:
             nsamp = min(64 * nw, batch - 64 * w0)
             L.call("clb_packed_layer_count", L.ptr(src), ld_src, nw, L.ptr(last.sel_ab), L.ptr(last.sel_gate),
                    last.n_out, self.k, self.class_size, L.ptr(counts), 64 * w0, nsamp, s)
+            n += len(self.layers)
+        self.launches_per_pass = n
+
+    @torch.no_grad()
+    def counts_packed(self, xw: torch.Tensor, batch: int, counts: Optional[torch.Tensor] = None,
+                      use_graph: Optional[bool] = None) -> torch.Tensor:
+        """Class counts [batch, k] of pre-packed inputs xw [features, W] (int64 words, unit column stride).
+
+        With graphs enabled (default) the pass — thousands of launches for large batches — is captured
+        once per (input, output) buffer pair into a CUDA graph and replayed, so the host issues one
+        launch per pass."""
+        if xw.shape[0] != self.in_features or (xw.shape[1] > 1 and xw.stride(1) != 1):
+            raise ValueError("xw must be [in_features, words] with unit column stride")
+        if counts is None:
+            counts = torch.empty(batch, self.k, dtype=torch.int32, device=self.device)
+        if not (self.use_graphs if use_graph is None else use_graph):
+            self._run(xw, batch, counts)
+            return counts
+        key = (xw.data_ptr(), tuple(xw.shape), xw.stride(0), batch, counts.data_ptr())
+        graph = self._graphs.get(key)
+        if graph is None:
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):  # eager warm-up allocates the chunk buffers outside the capture
+                self._run(xw, batch, counts)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._run(xw, batch, counts)
+            if len(self._graphs) >= 8:
+                self._graphs.pop(next(iter(self._graphs)))
+            self._graphs[key] = graph
+        graph.replay()
         return counts
 
     @torch.no_grad()
