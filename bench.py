@@ -363,11 +363,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--chunk-words", type=int, default=16)
     ap.add_argument("--layers", type=int, default=None, help="override the c2 depth (profiling on a smaller case)")
+    ap.add_argument("--samples", type=int, default=None, help="override the c4 sample count (profiling)")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work per baseline sample")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.layers:
         C2["layers"] = args.layers
+    if args.samples:
+        C4["samples"] = args.samples
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -71,12 +71,65 @@ __device__ __forceinline__ int2 used_operands(int2 s, const GatePoly& gp) {
 __device__ __forceinline__ float exp_acc(float v) { return expf(v); }
 __device__ __forceinline__ double exp_acc(double v) { return exp(v); }
 
-// Fill the stage for neurons [j0, j0+TN).  One thread per neuron; K is small (4..64).
+template <typename A> __device__ __forceinline__ A seg_max(A v, int K) {
+    for (int o = K >> 1; o > 0; o >>= 1) {
+        const A other = __shfl_xor_sync(0xffffffffu, v, o);
+        v = other > v ? other : v;
+    }
+    return v;
+}
+template <typename A> __device__ __forceinline__ A seg_sum(A v, int K) {
+    for (int o = K >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Fill the stage for neurons [j0, j0+TN).
+// K a power of two <= 32 (the usual 4 / 8 / 16): one thread per slot, the K slots of a neuron in K
+// adjacent lanes, softmax max/sum and the constant term by segmented warp reductions, so all
+// threads of the CTA share the staging work.  Otherwise, and in select mode: one thread per neuron.
 template <typename A, bool BACKWARD>
 __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) {
     const int K = a.K;
     const A* w = reinterpret_cast<const A*>(a.weights);
     const int2* slots = reinterpret_cast<const int2*>(a.slots);
+    if (a.mode != CLB_W_SELECT && K <= 32 && (K & (K - 1)) == 0) {
+        const int total = TN * K;
+        const int rounds = (total + blockDim.x - 1) / blockDim.x;
+        for (int it = 0; it < rounds; ++it) {
+            const int e = it * blockDim.x + threadIdx.x;  // warp-uniform trip count keeps the shuffles legal
+            const int t = e / K, k = e - t * K;
+            const int64_t j = j0 + t;
+            const bool valid = e < total && j < a.n_out;
+            const int64_t r = valid ? j / a.group : 0;
+            A p = 0;
+            if (a.mode == CLB_W_LOGITS) {
+                const A wv = valid ? w[r * K + k] : -(A)FLT_MAX;
+                const A m = seg_max(wv, K);
+                const A ex = valid ? exp_acc(wv - m) : (A)0;
+                const A sum = seg_sum(ex, K);
+                p = valid ? ex / sum : (A)0;
+            } else if (valid && w != nullptr) {
+                p = w[r * K + k];
+            }
+            GatePoly gp{0.f, 0.f, 0.f, 0.f};
+            if (valid) {
+                gp = gate_poly(a.gates[r * K + k] & 15);
+                st.ab[e] = used_operands(slots[j * K + k], gp);
+                if (BACKWARD) {
+                    st.cf[e] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
+                    st.p[e] = p;
+                } else {
+                    st.cf[e] = A4<A>{p * (A)gp.c1, p * (A)gp.c2, p * (A)gp.c3, (A)0};
+                }
+            }
+            const A c0sum = seg_sum(p * (A)gp.c0, K);
+            if (e < total && k == 0) {
+                st.ns[t] = valid ? K : 0;
+                if (!BACKWARD) st.c0[t] = c0sum;
+            }
+        }
+        return;
+    }
     for (int t = threadIdx.x; t < TN; t += blockDim.x) {
         const int64_t j = j0 + t;
         int ns = 0;

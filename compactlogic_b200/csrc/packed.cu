@@ -32,14 +32,12 @@ __device__ __forceinline__ void csa(uint64_t& h, uint64_t& l, uint64_t a, uint64
     l = u ^ c;
 }
 
+// 64 bit-sliced counters of 8 bits (counts up to 255): ones/twos/fours/eights are the Harley-Seal
+// state, hi[0..3] count the 16s.  A thread adds at most kMaxWords words.
 struct VCounter {
-    static constexpr int kPlanes = 20;  // counts of 16-word groups up to 2^20 - 1
+    static constexpr int kMaxWords = 240;
     uint64_t ones = 0, twos = 0, fours = 0, eights = 0;
-    uint64_t hi[kPlanes];
-    __device__ __forceinline__ VCounter() {
-#pragma unroll
-        for (int p = 0; p < kPlanes; ++p) hi[p] = 0;
-    }
+    uint64_t hi[4] = {0, 0, 0, 0};
     // Add 16 words.
     __device__ __forceinline__ void add16(const uint64_t (&d)[16]) {
         uint64_t twosA, twosB, foursA, foursB, eightsA, eightsB, sixteens;
@@ -60,19 +58,32 @@ struct VCounter {
         csa(sixteens, eights, eights, eightsA, eightsB);
         uint64_t carry = sixteens;
 #pragma unroll
-        for (int p = 0; p < kPlanes; ++p) {
+        for (int p = 0; p < 4; ++p) {
             const uint64_t t = hi[p] & carry;
             hi[p] ^= carry;
             carry = t;
         }
     }
-    __device__ __forceinline__ int value(int i) const {
-        int v = (int)((ones >> i) & 1) + 2 * (int)((twos >> i) & 1) + 4 * (int)((fours >> i) & 1) +
-                8 * (int)((eights >> i) & 1);
-        int h = 0;
-#pragma unroll
-        for (int p = 0; p < kPlanes; ++p) h |= (int)((hi[p] >> i) & 1) << p;
-        return v + 16 * h;
+    // 8x8 bit-matrix transpose: in byte r / bit c -> out byte c / bit r.
+    static __device__ __forceinline__ uint64_t transpose8x8(uint64_t x) {
+        uint64_t t;
+        t = (x ^ (x >> 7)) & 0x00AA00AA00AA00AAull;
+        x = x ^ t ^ (t << 7);
+        t = (x ^ (x >> 14)) & 0x0000CCCC0000CCCCull;
+        x = x ^ t ^ (t << 14);
+        t = (x ^ (x >> 28)) & 0x00000000F0F0F0F0ull;
+        x = x ^ t ^ (t << 28);
+        return x;
+    }
+    // Counts of positions 8m .. 8m+7 as the 8 bytes of one word: byte q of the gathered word is byte m
+    // of plane q; after the transpose byte r holds the 8-bit count of position 8m + r.
+    __device__ __forceinline__ uint64_t counts8(int m) const {
+        const int sh = 8 * m;
+        const uint64_t x = ((ones >> sh) & 0xff) | (((twos >> sh) & 0xff) << 8) | (((fours >> sh) & 0xff) << 16) |
+                           (((eights >> sh) & 0xff) << 24) | (((hi[0] >> sh) & 0xff) << 32) |
+                           (((hi[1] >> sh) & 0xff) << 40) | (((hi[2] >> sh) & 0xff) << 48) |
+                           (((hi[3] >> sh) & 0xff) << 56);
+        return transpose8x8(x);
     }
 };
 
@@ -84,17 +95,6 @@ __device__ __forceinline__ uint64_t load_word_bytes(const uint8_t* __restrict__ 
     for (int b = 0; b < 8; ++b)
         if (off + b < row_bytes) v |= (uint64_t)row[off + b] << (8 * b);
     return v;
-}
-
-// Flush a counter for word column w into counts[(sample0 + 64 w + i) * k + c], i < 64.
-__device__ __forceinline__ void flush_counts(const VCounter& vc, int64_t w, int64_t c, int64_t k, int64_t samples,
-                                             int32_t* __restrict__ counts, int64_t sample0) {
-    for (int i = 0; i < 64; ++i) {
-        const int64_t n = 64 * w + i;
-        if (n >= samples) break;
-        const int v = vc.value(i);
-        if (v) atomicAdd(counts + (sample0 + n) * k + c, v);
-    }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -116,32 +116,6 @@ __global__ void packbits_kernel(const uint8_t* __restrict__ t, int64_t rows, int
             const int64_t byte = blk * 4 + lane;
             if (byte < row_bytes) out[r * row_bytes + byte] = (uint8_t)(word >> (8 * lane));
         }
-    }
-}
-
-// groupbitsum: counts[n, c] += sum over rows of class c of bit n.  One thread per
-// (class, segment of rows, 64-sample word column); lanes run over word columns.
-__global__ void groupbitsum_kernel(const uint8_t* __restrict__ words, int64_t rows, int64_t row_bytes,
-                                   int64_t samples, int64_t k, int64_t class_size, int64_t nseg, int64_t seg_len,
-                                   int32_t* __restrict__ counts, int64_t sample0) {
-    const int64_t W = (row_bytes + 7) / 8;
-    const int64_t total = k * nseg * W;
-    const bool al8 = (row_bytes % 8) == 0 && ((uintptr_t)words % 8) == 0;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t w = e % W;
-        const int64_t cs = e / W;
-        const int64_t seg = cs % nseg, c = cs / nseg;
-        const int64_t r0 = c * class_size + seg * seg_len;
-        const int64_t r1 = min(min(r0 + seg_len, (c + 1) * class_size), rows);
-        VCounter vc;
-        for (int64_t r = r0; r < r1; r += 16) {
-            uint64_t d[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-                d[q] = (r + q < r1) ? load_word_bytes(words + (r + q) * row_bytes, 8 * w, row_bytes, al8) : 0ull;
-            vc.add16(d);
-        }
-        flush_counts(vc, w, c, k, samples, counts, sample0);
     }
 }
 
@@ -230,36 +204,86 @@ packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords,
     }
 }
 
-// Final packed layer fused with the packed GroupSum: computes each neuron's word and feeds it
-// straight into the vertical counter of its class, never storing the layer output.
+// ------------------------------------------------------------------------------------------
+// Packed GroupSum: counts[(sample0 + 64 w + i) * k + c] += #{rows r of class c : bit i of word(r, w)}.
+// A CTA owns one class, a tile of TW word columns and S = 256/TW row segments of up to 240 rows:
+// thread (segment, column) runs a vertical counter over its rows, the CTA folds the S counters in
+// shared memory (four 16-bit counts per 64-bit shared atomic), then adds each nonzero
+// (column, position) total to global memory once.  `Src` yields word(r, w): a stored packed row
+// (groupbitsum) or, for the fused last layer, the gate output computed on the fly.
+// ------------------------------------------------------------------------------------------
+struct RowWords {
+    const uint8_t* words;
+    int64_t row_bytes;
+    bool al8;
+    __device__ __forceinline__ uint64_t operator()(int64_t r, int64_t w) const {
+        return load_word_bytes(words + r * row_bytes, 8 * w, row_bytes, al8);
+    }
+};
+
+struct GateWords {
+    const uint64_t* x;
+    int64_t ldx;
+    const int2* ab;
+    const uint8_t* gate;
+    __device__ __forceinline__ uint64_t operator()(int64_t j, int64_t w) const {
+        const int2 p = ab[j];
+        return gate_word<uint64_t>(gate[j], word_or_zero(x, p.x, ldx, w), word_or_zero(x, p.y, ldx, w));
+    }
+};
+
+struct CountPlan {
+    int tw_log2;      // columns per CTA = 1 << tw_log2
+    int64_t seg_len;  // rows per thread (multiple of 16, <= 240)
+    int64_t nseg;     // segments per class
+    int64_t groups;   // CTAs per (class, column tile) = ceil(nseg / S)
+};
+
+template <class Src>
 __global__ void __launch_bounds__(256)
-packed_layer_count_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
-                          const uint8_t* __restrict__ sel_gate, int64_t n_out, int64_t k, int64_t class_size,
-                          int64_t nseg, int64_t seg_len, int32_t* __restrict__ counts, int64_t sample0,
-                          int64_t samples) {
-    const int64_t total = k * nseg * nwords;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t w = e % nwords;
-        const int64_t cs = e / nwords;
-        const int64_t seg = cs % nseg, c = cs / nseg;
-        const int64_t j0 = c * class_size + seg * seg_len;
-        const int64_t j1 = min(min(j0 + seg_len, (c + 1) * class_size), n_out);
+count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int64_t k, const int64_t class_size,
+             const CountPlan plan, int32_t* __restrict__ counts, const int64_t sample0, const int64_t samples) {
+    __shared__ unsigned long long s_cnt[32 * 16];  // [column][position / 4], four 16-bit lanes each
+    const int TW = 1 << plan.tw_log2;
+    const int S = 256 >> plan.tw_log2;
+    const int wl = threadIdx.x & (TW - 1), sl = threadIdx.x >> plan.tw_log2;
+    for (int i = threadIdx.x; i < TW * 16; i += blockDim.x) s_cnt[i] = 0;
+    __syncthreads();
+    const int64_t c = blockIdx.y / plan.groups;
+    const int64_t seg = (blockIdx.y - c * plan.groups) * S + sl;
+    const int64_t w = (int64_t)blockIdx.x * TW + wl;
+    if (w < nwords && seg < plan.nseg) {
+        const int64_t r0 = c * class_size + seg * plan.seg_len;
+        const int64_t r1 = min(min(r0 + plan.seg_len, (c + 1) * class_size), rows);
         VCounter vc;
-        for (int64_t j = j0; j < j1; j += 16) {
+        for (int64_t r = r0; r < r1; r += 16) {
             uint64_t d[16];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                uint64_t v = 0;
-                if (j + q < j1) {
-                    const int2 ab = sel_ab[j + q];
-                    v = gate_word<uint64_t>(sel_gate[j + q], word_or_zero(x, ab.x, ldx, w),
-                                            word_or_zero(x, ab.y, ldx, w));
-                }
-                d[q] = v;
-            }
+            for (int q = 0; q < 16; ++q) d[q] = (r + q < r1) ? src(r + q, w) : 0ull;
             vc.add16(d);
         }
-        flush_counts(vc, w, c, k, samples, counts, sample0);
+#pragma unroll 1
+        for (int m = 0; m < 8; ++m) {
+            const uint64_t v8 = vc.counts8(m);
+            if (v8 == 0) continue;
+            // widen 8 x 8-bit counts to 2 x (4 x 16-bit) and add them to the CTA totals
+            unsigned long long lo = 0, hi = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                lo |= ((v8 >> (8 * q)) & 0xffull) << (16 * q);
+                hi |= ((v8 >> (8 * q + 32)) & 0xffull) << (16 * q);
+            }
+            if (lo) atomicAdd(&s_cnt[wl * 16 + 2 * m], lo);
+            if (hi) atomicAdd(&s_cnt[wl * 16 + 2 * m + 1], hi);
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < TW * 64; e += blockDim.x) {
+        const int col = e >> 6, pos = e & 63;
+        const int64_t ww = (int64_t)blockIdx.x * TW + col;
+        const int v = (int)((s_cnt[col * 16 + (pos >> 2)] >> (16 * (pos & 3))) & 0xffff);
+        const int64_t n = 64 * ww + pos;
+        if (v && ww < nwords && n < samples) atomicAdd(counts + (sample0 + n) * k + c, v);
     }
 }
 
@@ -267,12 +291,33 @@ unsigned grid_for(int64_t threads) {
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(threads, 256), (int64_t)148 * 32));
 }
 
-// Enough (class, segment, word) threads to fill the GPU, segments of at least 64 rows.
-void choose_segments(int64_t k, int64_t class_size, int64_t W, int64_t& nseg, int64_t& seg_len) {
-    const int64_t target = 148 * 2048;
-    nseg = std::max<int64_t>(1, std::min<int64_t>(ceil_div64(class_size, 64), ceil_div64(target, std::max<int64_t>(1, k * W))));
-    seg_len = ceil_div64(class_size, nseg);
-    nseg = ceil_div64(class_size, seg_len);
+// Segments as long as possible (fewer flushes) while keeping ~150 K threads; every thread keeps 16-32
+// independent loads in flight, so this hides the L2 latency.
+CountPlan plan_count(int64_t k, int64_t class_size, int64_t W) {
+    CountPlan p{};
+    p.tw_log2 = 0;
+    while ((1 << p.tw_log2) < W && p.tw_log2 < 5) ++p.tw_log2;
+    const int64_t target = 148 * 1024;
+    int64_t len = ceil_div64(std::max<int64_t>(1, class_size * k * W), target);
+    len = std::min<int64_t>(VCounter::kMaxWords, std::max<int64_t>(16, ceil_div64(len, 16) * 16));
+    for (;;) {
+        p.seg_len = len;
+        p.nseg = ceil_div64(class_size, len);
+        p.groups = ceil_div64(p.nseg, 256 >> p.tw_log2);
+        if (k * p.groups <= 65535 || len >= VCounter::kMaxWords) break;
+        len = std::min<int64_t>(VCounter::kMaxWords, len + 16);
+    }
+    return p;
+}
+
+template <class Src>
+cudaError_t launch_count(const Src& src, int64_t rows, int64_t nwords, int64_t k, int64_t class_size,
+                         int32_t* counts, int64_t sample0, int64_t samples, cudaStream_t s) {
+    const CountPlan p = plan_count(k, class_size, nwords);
+    if (k * p.groups > 65535) return cudaErrorInvalidConfiguration;
+    dim3 grid((unsigned)ceil_div64(nwords, 1 << p.tw_log2), (unsigned)(k * p.groups));
+    count_kernel<Src><<<grid, 256, 0, s>>>(src, rows, nwords, k, class_size, p, counts, sample0, samples);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -294,12 +339,8 @@ cudaError_t launch_groupbitsum(const uint8_t* words, int64_t rows, int64_t row_b
         if (e != cudaSuccess) return e;
     }
     if (rows == 0 || samples == 0 || k == 0) return cudaSuccess;
-    const int64_t W = (row_bytes + 7) / 8;
-    int64_t nseg, seg_len;
-    choose_segments(k, class_size, W, nseg, seg_len);
-    groupbitsum_kernel<<<grid_for(k * nseg * W), 256, 0, s>>>(words, rows, row_bytes, samples, k, class_size, nseg,
-                                                              seg_len, counts, sample0);
-    return cudaGetLastError();
+    const RowWords src{words, row_bytes, (row_bytes % 8) == 0 && ((uintptr_t)words % 8) == 0};
+    return launch_count(src, rows, (row_bytes + 7) / 8, k, class_size, counts, sample0, samples, s);
 }
 
 cudaError_t launch_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx,
@@ -344,12 +385,8 @@ cudaError_t launch_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nw
                                       const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size,
                                       int32_t* counts, int64_t sample0, int64_t nsamples, cudaStream_t s) {
     if (n_out == 0 || nwords == 0 || k == 0) return cudaSuccess;
-    int64_t nseg, seg_len;
-    choose_segments(k, class_size, nwords, nseg, seg_len);
-    packed_layer_count_kernel<<<grid_for(k * nseg * nwords), 256, 0, s>>>(
-        x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate, n_out, k, class_size, nseg, seg_len, counts,
-        sample0, nsamples);
-    return cudaGetLastError();
+    const GateWords src{x, ldx, reinterpret_cast<const int2*>(sel_ab), sel_gate};
+    return launch_count(src, n_out, nwords, k, class_size, counts, sample0, nsamples, s);
 }
 
 }  // namespace clb
