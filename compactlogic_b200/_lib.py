@@ -58,7 +58,8 @@ _SIGS = {
     "clb_pack_inputs": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "clb_packed_select": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _p]),
     "clb_packed_layer": (_int, [_p, _i64, _i64, _p, _p, _i64, _p, _i64, _p]),
-    "clb_packed_layer_count": (_int, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _i64, _p]),
+    "clb_packed_count_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "clb_packed_layer_count": (_int, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _sz, _p]),
     "clb_packed_count": (_int, [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p]),
 }
 

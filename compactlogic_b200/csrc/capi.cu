@@ -245,17 +245,24 @@ int clb_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32
     return cuda_status(launch_packed_layer(x, ldx, nwords, sel_ab, sel_gate, n_out, y, ldy, S(stream)), "packed_layer");
 }
 
+size_t clb_packed_count_workspace_bytes(int64_t k, int64_t class_size, int64_t nwords) {
+    if (k < 1 || class_size < 1 || nwords < 1) return 0;
+    return packed_count_workspace_bytes(k, class_size, nwords);
+}
+
 int clb_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
                            const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size, int32_t* counts,
-                           int64_t sample0, int64_t nsamples, clb_stream_t stream) {
+                           int64_t sample0, int64_t nsamples, void* workspace, size_t workspace_bytes,
+                           clb_stream_t stream) {
     if (nwords < 0 || n_out < 0 || ldx < nwords || k < 1 || class_size < 1 || sample0 < 0 || nsamples < 0 ||
         nsamples > 64 * nwords)
         return fail(CLB_ERR_INVALID, "packed_layer_count: sizes");
     if (nwords * n_out > 0 && (!x || !sel_ab || !sel_gate || !counts))
         return fail(CLB_ERR_INVALID, "packed_layer_count: null");
+    const int kernels = workspace ? 2 : 1;
     return cuda_status(launch_packed_layer_count(x, ldx, nwords, sel_ab, sel_gate, n_out, k, class_size, counts, sample0,
-                                                 nsamples, S(stream)),
-                       "packed_layer_count");
+                                                 nsamples, workspace, workspace_bytes, S(stream)),
+                       "packed_layer_count", kernels);
 }
 
 int clb_packed_count(const uint64_t* words, int64_t rows, int64_t nwords, int64_t k, int64_t class_size,

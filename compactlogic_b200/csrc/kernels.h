@@ -86,7 +86,9 @@ cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, 
                                 const uint8_t* sel_gate, int64_t n_out, uint64_t* y, int64_t ldy, cudaStream_t s);
 cudaError_t launch_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
                                       const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size,
-                                      int32_t* counts, int64_t sample0, int64_t nsamples, cudaStream_t s);
+                                      int32_t* counts, int64_t sample0, int64_t nsamples, void* ws, size_t ws_bytes,
+                                      cudaStream_t s);
+size_t packed_count_workspace_bytes(int64_t k, int64_t class_size, int64_t nwords);
 
 // Error / launch bookkeeping of the C ABI (capi.cu), for entry points defined in other files.
 int set_error(int code, const char* msg);

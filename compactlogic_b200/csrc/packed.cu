@@ -239,10 +239,13 @@ struct CountPlan {
     int64_t groups;   // CTAs per (class, column tile) = ceil(nseg / S)
 };
 
+// partial != null: instead of atomics into counts, the CTA stores its totals (zeros included) to
+// partial[blockIdx.y][64 * w + pos] (row length 64 * gridDim.x * TW) and sum_partials folds them.
 template <class Src>
 __global__ void __launch_bounds__(256)
 count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int64_t k, const int64_t class_size,
-             const CountPlan plan, int32_t* __restrict__ counts, const int64_t sample0, const int64_t samples) {
+             const CountPlan plan, int32_t* __restrict__ counts, const int64_t sample0, const int64_t samples,
+             int32_t* __restrict__ partial) {
     __shared__ unsigned long long s_cnt[32 * 16];  // [column][position / 4], four 16-bit lanes each
     const int TW = 1 << plan.tw_log2;
     const int S = 256 >> plan.tw_log2;
@@ -283,7 +286,21 @@ count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int6
         const int64_t ww = (int64_t)blockIdx.x * TW + col;
         const int v = (int)((s_cnt[col * 16 + (pos >> 2)] >> (16 * (pos & 3))) & 0xffff);
         const int64_t n = 64 * ww + pos;
-        if (v && ww < nwords && n < samples) atomicAdd(counts + (sample0 + n) * k + c, v);
+        if (partial != nullptr)
+            partial[(int64_t)blockIdx.y * (64 * (int64_t)gridDim.x * TW) + n] = v;
+        else if (v && ww < nwords && n < samples)
+            atomicAdd(counts + (sample0 + n) * k + c, v);
+    }
+}
+
+// counts[(sample0 + n) * k + c] += sum_g partial[c * groups + g][n]   (one writer per element)
+__global__ void sum_partials_kernel(const int32_t* __restrict__ partial, int64_t row, int64_t groups, int64_t k,
+                                    int32_t* __restrict__ counts, int64_t sample0, int64_t samples) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < samples * k; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = e / samples, n = e - c * samples;
+        int32_t v = 0;
+        for (int64_t g = 0; g < groups; ++g) v += partial[(c * groups + g) * row + n];
+        counts[(sample0 + n) * k + c] += v;
     }
 }
 
@@ -293,11 +310,13 @@ unsigned grid_for(int64_t threads) {
 
 // Segments as long as possible (fewer flushes) while keeping ~150 K threads; every thread keeps 16-32
 // independent loads in flight, so this hides the L2 latency.
-CountPlan plan_count(int64_t k, int64_t class_size, int64_t W) {
+CountPlan plan_count(int64_t k, int64_t class_size, int64_t W, bool to_partial) {
     CountPlan p{};
     p.tw_log2 = 0;
     while ((1 << p.tw_log2) < W && p.tw_log2 < 5) ++p.tw_log2;
-    const int64_t target = 148 * 1024;
+    // with atomics every CTA of a class hits the same counters, so fewer, longer segments pay off;
+    // with the partials there is no contention and more threads hide the gather latency better
+    const int64_t target = to_partial ? 148 * 2048 : 148 * 1024;
     int64_t len = ceil_div64(std::max<int64_t>(1, class_size * k * W), target);
     len = std::min<int64_t>(VCounter::kMaxWords, std::max<int64_t>(16, ceil_div64(len, 16) * 16));
     for (;;) {
@@ -312,11 +331,25 @@ CountPlan plan_count(int64_t k, int64_t class_size, int64_t W) {
 
 template <class Src>
 cudaError_t launch_count(const Src& src, int64_t rows, int64_t nwords, int64_t k, int64_t class_size,
-                         int32_t* counts, int64_t sample0, int64_t samples, cudaStream_t s) {
-    const CountPlan p = plan_count(k, class_size, nwords);
+                         int32_t* counts, int64_t sample0, int64_t samples, void* ws, size_t ws_bytes,
+                         cudaStream_t s) {
+    CountPlan p = plan_count(k, class_size, nwords, ws != nullptr);
+    const int64_t tiles = ceil_div64(nwords, 1 << p.tw_log2);
+    const int64_t row = 64 * tiles * (1 << p.tw_log2);
+    int32_t* partial = nullptr;
+    if (ws != nullptr) {
+        if ((size_t)(k * p.groups * row) * sizeof(int32_t) > ws_bytes) {
+            p = plan_count(k, class_size, nwords, false);  // workspace too small: atomics
+        } else {
+            partial = reinterpret_cast<int32_t*>(ws);
+        }
+    }
     if (k * p.groups > 65535) return cudaErrorInvalidConfiguration;
-    dim3 grid((unsigned)ceil_div64(nwords, 1 << p.tw_log2), (unsigned)(k * p.groups));
-    count_kernel<Src><<<grid, 256, 0, s>>>(src, rows, nwords, k, class_size, p, counts, sample0, samples);
+    dim3 grid((unsigned)tiles, (unsigned)(k * p.groups));
+    count_kernel<Src><<<grid, 256, 0, s>>>(src, rows, nwords, k, class_size, p, counts, sample0, samples, partial);
+    if (partial != nullptr) {
+        sum_partials_kernel<<<grid_for(samples * k), 256, 0, s>>>(partial, row, p.groups, k, counts, sample0, samples);
+    }
     return cudaGetLastError();
 }
 
@@ -340,7 +373,7 @@ cudaError_t launch_groupbitsum(const uint8_t* words, int64_t rows, int64_t row_b
     }
     if (rows == 0 || samples == 0 || k == 0) return cudaSuccess;
     const RowWords src{words, row_bytes, (row_bytes % 8) == 0 && ((uintptr_t)words % 8) == 0};
-    return launch_count(src, rows, (row_bytes + 7) / 8, k, class_size, counts, sample0, samples, s);
+    return launch_count(src, rows, (row_bytes + 7) / 8, k, class_size, counts, sample0, samples, nullptr, 0, s);
 }
 
 cudaError_t launch_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx,
@@ -383,10 +416,17 @@ cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, 
 
 cudaError_t launch_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
                                       const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size,
-                                      int32_t* counts, int64_t sample0, int64_t nsamples, cudaStream_t s) {
+                                      int32_t* counts, int64_t sample0, int64_t nsamples, void* ws, size_t ws_bytes,
+                                      cudaStream_t s) {
     if (n_out == 0 || nwords == 0 || k == 0) return cudaSuccess;
     const GateWords src{x, ldx, reinterpret_cast<const int2*>(sel_ab), sel_gate};
-    return launch_count(src, n_out, nwords, k, class_size, counts, sample0, nsamples, s);
+    return launch_count(src, n_out, nwords, k, class_size, counts, sample0, nsamples, ws, ws_bytes, s);
+}
+
+size_t packed_count_workspace_bytes(int64_t k, int64_t class_size, int64_t nwords) {
+    const CountPlan p = plan_count(k, class_size, nwords, true);
+    const int64_t row = 64 * ceil_div64(nwords, 1 << p.tw_log2) * (1 << p.tw_log2);
+    return (size_t)(k * p.groups * row) * sizeof(int32_t);
 }
 
 }  // namespace clb

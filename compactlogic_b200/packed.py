@@ -57,6 +57,7 @@ class PackedLogicNet:
         self.in_features = self.layers[0].in_features
         self.class_size = -(-self.layers[-1].n_out // self.k)
         self._bufs = None
+        self._ws = None
         self.use_graphs = True
         self._graphs = {}
         self.launches_per_pass = 0
@@ -96,6 +97,13 @@ class PackedLogicNet:
             self._bufs = tuple(torch.empty(rows, width, dtype=torch.int64, device=self.device) for _ in range(2))
         return self._bufs
 
+    def _count_ws(self, nwords: int) -> torch.Tensor:
+        """Workspace of the fused count (per-CTA partial totals, summed without atomics)."""
+        need = int(L.lib().clb_packed_count_workspace_bytes(self.k, self.class_size, nwords))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
+        return self._ws
+
     def _run(self, xw: torch.Tensor, batch: int, counts: torch.Tensor) -> None:
         """Enqueue one pass: per chunk, every layer then the fused last layer + class count."""
         W = xw.shape[1]
@@ -114,9 +122,10 @@ class PackedLogicNet:
                 src, ld_src = dst, dst.stride(0)
             last = self.layers[-1]
             nsamp = min(64 * nw, batch - 64 * w0)
+            ws = self._count_ws(nw)
             L.call("clb_packed_layer_count", L.ptr(src), ld_src, nw, L.ptr(last.sel_ab), L.ptr(last.sel_gate),
-                   last.n_out, self.k, self.class_size, L.ptr(counts), 64 * w0, nsamp, s)
-            n += len(self.layers)
+                   last.n_out, self.k, self.class_size, L.ptr(counts), 64 * w0, nsamp, L.ptr(ws), ws.numel(), s)
+            n += len(self.layers) + 1
         self.launches_per_pass = n
 
     @torch.no_grad()

@@ -235,10 +235,14 @@ int clb_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32
 
 /* Last packed layer fused with GroupSum: counts[(sample0 + n) * k + class] += number of neurons of the
  * class whose output bit for sample n is 1 (n < nsamples; class(j) = j / class_size).  counts int32
- * [*, k], accumulated (zero it first). */
+ * [*, k], accumulated (zero it first).  With a workspace of clb_packed_count_workspace_bytes() bytes
+ * the per-CTA totals go through the workspace and are summed by a second kernel (no atomics on
+ * counts, deterministic); with workspace == NULL (or too small) they are added atomically. */
+size_t clb_packed_count_workspace_bytes(int64_t k, int64_t class_size, int64_t nwords);
 int clb_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
                            const uint8_t* sel_gate, int64_t n_out, int64_t k, int64_t class_size, int32_t* counts,
-                           int64_t sample0, int64_t nsamples, clb_stream_t stream);
+                           int64_t sample0, int64_t nsamples, void* workspace, size_t workspace_bytes,
+                           clb_stream_t stream);
 
 /* Packed GroupSum over stored words [rows, nwords] uint64: same accumulation as above. */
 int clb_packed_count(const uint64_t* words, int64_t rows, int64_t nwords, int64_t k, int64_t class_size,
