@@ -167,16 +167,18 @@ __device__ __forceinline__ uint64_t word_or_zero(const uint64_t* __restrict__ x,
     return idx >= 0 ? __ldg(x + (int64_t)idx * ldx + w) : 0ull;
 }
 
-// One packed layer.  TW lanes span word columns, 32/TW neurons per warp, and each thread handles
-// R neurons spaced 32/TW apart so that 2R independent 8-byte loads are in flight per thread.
-template <int R>
+// One packed layer.  Each lane owns V consecutive word columns (V = 2: one 16-byte load per operand),
+// TW lanes span TW*V columns, 32/TW neurons share a warp row, and each thread handles R neurons
+// spaced 32/TW apart so that 2R independent loads are in flight per thread.
+template <int R, int V>
 __global__ void __launch_bounds__(256)
 packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
                     const uint8_t* __restrict__ sel_gate, int64_t n_out, uint64_t* __restrict__ y, int64_t ldy,
                     int tw_log2) {
+    using Vw = Vec<uint64_t, V>;
     const int TW = 1 << tw_log2;
     const int lane = threadIdx.x & 31;
-    const int64_t w = (int64_t)blockIdx.x * TW + (lane & (TW - 1));
+    const int64_t w = ((int64_t)blockIdx.x * TW + (lane & (TW - 1))) * V;
     const int64_t npw = 32 >> tw_log2;  // neurons per warp row
     const int64_t warp_global = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.y * blockDim.x) >> 5;
@@ -190,16 +192,23 @@ packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords,
             ab[q] = j < n_out ? sel_ab[j] : make_int2(-1, -1);
             g[q] = j < n_out ? sel_gate[j] : 0;
         }
-        uint64_t va[R], vb[R];
+        Vw va[R], vb[R];
 #pragma unroll
         for (int q = 0; q < R; ++q) {
-            va[q] = word_or_zero(x, ab[q].x, ldx, w);
-            vb[q] = word_or_zero(x, ab[q].y, ldx, w);
+#pragma unroll
+            for (int i = 0; i < V; ++i) va[q].v[i] = vb[q].v[i] = 0;
+            if (ab[q].x >= 0) va[q] = *reinterpret_cast<const Vw*>(x + (int64_t)ab[q].x * ldx + w);
+            if (ab[q].y >= 0) vb[q] = *reinterpret_cast<const Vw*>(x + (int64_t)ab[q].y * ldx + w);
         }
 #pragma unroll
         for (int q = 0; q < R; ++q) {
             const int64_t j = base + q * npw + (lane >> tw_log2);
-            if (j < n_out) y[j * ldy + w] = gate_word<uint64_t>(g[q], va[q], vb[q]);
+            if (j < n_out) {
+                Vw o;
+#pragma unroll
+                for (int i = 0; i < V; ++i) o.v[i] = gate_word<uint64_t>(g[q], va[q].v[i], vb[q].v[i]);
+                *reinterpret_cast<Vw*>(y + j * ldy + w) = o;
+            }
         }
     }
 }
@@ -216,8 +225,11 @@ struct RowWords {
     const uint8_t* words;
     int64_t row_bytes;
     bool al8;
-    __device__ __forceinline__ uint64_t operator()(int64_t r, int64_t w) const {
-        return load_word_bytes(words + r * row_bytes, 8 * w, row_bytes, al8);
+    // rows r .. r+15 (zero at and beyond r1)
+    __device__ __forceinline__ void load16(int64_t r, int64_t r1, int64_t w, uint64_t (&d)[16]) const {
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+            d[q] = (r + q < r1) ? load_word_bytes(words + (r + q) * row_bytes, 8 * w, row_bytes, al8) : 0ull;
     }
 };
 
@@ -226,9 +238,28 @@ struct GateWords {
     int64_t ldx;
     const int2* ab;
     const uint8_t* gate;
-    __device__ __forceinline__ uint64_t operator()(int64_t j, int64_t w) const {
-        const int2 p = ab[j];
-        return gate_word<uint64_t>(gate[j], word_or_zero(x, p.x, ldx, w), word_or_zero(x, p.y, ldx, w));
+    // neurons j .. j+15 (zero at and beyond j1): all table loads first, then the gathers 8 at a time,
+    // so the dependent loads of 8 neurons are in flight together
+    __device__ __forceinline__ void load16(int64_t j, int64_t j1, int64_t w, uint64_t (&d)[16]) const {
+        int2 p[16];
+        int g[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            const int64_t jj = j + q < j1 ? j + q : j1 - 1;
+            p[q] = ab[jj];
+            g[q] = gate[jj];
+        }
+#pragma unroll
+        for (int h = 0; h < 16; h += 8) {
+            uint64_t va[8], vb[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                va[q] = word_or_zero(x, p[h + q].x, ldx, w);
+                vb[q] = word_or_zero(x, p[h + q].y, ldx, w);
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) d[h + q] = (j + h + q < j1) ? gate_word<uint64_t>(g[h + q], va[q], vb[q]) : 0ull;
+        }
     }
 };
 
@@ -261,8 +292,7 @@ count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int6
         VCounter vc;
         for (int64_t r = r0; r < r1; r += 16) {
             uint64_t d[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) d[q] = (r + q < r1) ? src(r + q, w) : 0ull;
+            src.load16(r, r1, w, d);
             vc.add16(d);
         }
 #pragma unroll 1
@@ -401,16 +431,23 @@ cudaError_t launch_packed_select(const int32_t* slots, const uint8_t* gates, con
 cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
                                 const uint8_t* sel_gate, int64_t n_out, uint64_t* y, int64_t ldy, cudaStream_t s) {
     if (n_out == 0 || nwords == 0) return cudaSuccess;
+    const bool v2 = nwords % 2 == 0 && ldx % 2 == 0 && ldy % 2 == 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0;
+    const int V = v2 ? 2 : 1;
+    const int64_t cols = nwords / V;  // lane-owned column groups
     int tw_log2 = 0;
-    while ((1 << tw_log2) < nwords && tw_log2 < 5) ++tw_log2;
+    while ((1 << tw_log2) < cols && tw_log2 < 5) ++tw_log2;
     const int64_t TW = 1 << tw_log2;
     const int64_t npw = 32 / TW;
     constexpr int R = 4;
     const int64_t warps_needed = ceil_div64(n_out, npw * R);
     const int64_t by = std::min<int64_t>(ceil_div64(warps_needed, 8), 65535);
-    dim3 grid((unsigned)ceil_div64(nwords, TW), (unsigned)by);
-    packed_layer_kernel<R><<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate, n_out,
-                                                y, ldy, tw_log2);
+    dim3 grid((unsigned)ceil_div64(cols, TW), (unsigned)by);
+    if (v2)
+        packed_layer_kernel<R, 2><<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate,
+                                                       n_out, y, ldy, tw_log2);
+    else
+        packed_layer_kernel<R, 1><<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate,
+                                                       n_out, y, ldy, tw_log2);
     return cudaGetLastError();
 }
 
