@@ -277,49 +277,58 @@ __global__ void __launch_bounds__(256)
 count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int64_t k, const int64_t class_size,
              const CountPlan plan, int32_t* __restrict__ counts, const int64_t sample0, const int64_t samples,
              int32_t* __restrict__ partial) {
-    __shared__ unsigned long long s_cnt[32 * 16];  // [column][position / 4], four 16-bit lanes each
+    // [thread][position / 4]: each thread's 64 counts as four 16-bit lanes per word, no atomics
+    __shared__ unsigned long long s_cnt[256 * 16];
     const int TW = 1 << plan.tw_log2;
     const int S = 256 >> plan.tw_log2;
     const int wl = threadIdx.x & (TW - 1), sl = threadIdx.x >> plan.tw_log2;
-    for (int i = threadIdx.x; i < TW * 16; i += blockDim.x) s_cnt[i] = 0;
-    __syncthreads();
     const int64_t c = blockIdx.y / plan.groups;
     const int64_t seg = (blockIdx.y - c * plan.groups) * S + sl;
     const int64_t w = (int64_t)blockIdx.x * TW + wl;
+    VCounter vc;
     if (w < nwords && seg < plan.nseg) {
         const int64_t r0 = c * class_size + seg * plan.seg_len;
         const int64_t r1 = min(min(r0 + plan.seg_len, (c + 1) * class_size), rows);
-        VCounter vc;
         for (int64_t r = r0; r < r1; r += 16) {
             uint64_t d[16];
             src.load16(r, r1, w, d);
             vc.add16(d);
         }
-#pragma unroll 1
-        for (int m = 0; m < 8; ++m) {
-            const uint64_t v8 = vc.counts8(m);
-            if (v8 == 0) continue;
-            // widen 8 x 8-bit counts to 2 x (4 x 16-bit) and add them to the CTA totals
-            unsigned long long lo = 0, hi = 0;
+    }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                lo |= ((v8 >> (8 * q)) & 0xffull) << (16 * q);
-                hi |= ((v8 >> (8 * q + 32)) & 0xffull) << (16 * q);
-            }
-            if (lo) atomicAdd(&s_cnt[wl * 16 + 2 * m], lo);
-            if (hi) atomicAdd(&s_cnt[wl * 16 + 2 * m + 1], hi);
+    for (int m = 0; m < 8; ++m) {
+        const uint64_t v8 = vc.counts8(m);
+        unsigned long long lo = 0, hi = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            lo |= ((v8 >> (8 * q)) & 0xffull) << (16 * q);
+            hi |= ((v8 >> (8 * q + 32)) & 0xffull) << (16 * q);
         }
+        // slot index rotated by the thread id so the 16 stores of a warp spread over the banks
+        s_cnt[threadIdx.x * 16 + ((2 * m + threadIdx.x) & 15)] = lo;
+        s_cnt[threadIdx.x * 16 + ((2 * m + 1 + threadIdx.x) & 15)] = hi;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < TW * 64; e += blockDim.x) {
-        const int col = e >> 6, pos = e & 63;
+    // fold the S segments of each (column, 4-position group): packed 16-bit adds cannot overflow
+    // (at most 256 * 240 < 65536 per lane)
+    for (int e = threadIdx.x; e < TW * 16; e += blockDim.x) {
+        const int col = e >> 4, grp = e & 15;
+        unsigned long long acc = 0;
+        for (int t2 = 0; t2 < S; ++t2) {
+            const int tid = t2 * TW + col;
+            acc += s_cnt[tid * 16 + ((grp + tid) & 15)];
+        }
         const int64_t ww = (int64_t)blockIdx.x * TW + col;
-        const int v = (int)((s_cnt[col * 16 + (pos >> 2)] >> (16 * (pos & 3))) & 0xffff);
-        const int64_t n = 64 * ww + pos;
-        if (partial != nullptr)
-            partial[(int64_t)blockIdx.y * (64 * (int64_t)gridDim.x * TW) + n] = v;
-        else if (v && ww < nwords && n < samples)
-            atomicAdd(counts + (sample0 + n) * k + c, v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int pos = grp * 4 + q;
+            const int v = (int)((acc >> (16 * q)) & 0xffff);
+            const int64_t n = 64 * ww + pos;
+            if (partial != nullptr)
+                partial[(int64_t)blockIdx.y * (64 * (int64_t)gridDim.x * TW) + n] = v;
+            else if (v && ww < nwords && n < samples)
+                atomicAdd(counts + (sample0 + n) * k + c, v);
+        }
     }
 }
 
