@@ -361,7 +361,7 @@ def main():
     ap.add_argument("--workload", default="c2", choices=["c2", "c4"])
     ap.add_argument("--no-packed", action="store_true", help="skip the packed-inference (c4) sub-measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    ap.add_argument("--chunk-words", type=int, default=16)
+    ap.add_argument("--chunk-words", type=int, default=128)
     ap.add_argument("--layers", type=int, default=None, help="override the c2 depth (profiling on a smaller case)")
     ap.add_argument("--samples", type=int, default=None, help="override the c4 sample count (profiling)")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work per baseline sample")

@@ -16,6 +16,9 @@
 // coefficients are computed once per CTA into shared memory and read back as broadcasts.
 #include <cuda_runtime.h>
 #include <float.h>
+#include <stdlib.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "gates.cuh"
@@ -587,6 +590,21 @@ int choose_tn(size_t bytes_per_neuron) {
 
 template <typename T> constexpr int vmax() { return 16 / (int)sizeof(T); }
 
+// fp32 vector width of the forward / backward column split (4 = 128 columns per CTA, 2 = 64); the
+// environment variables CLB_FWD_VEC / CLB_BWD_VEC select 2 for tuning, read once per process.
+int env_vec(const char* name) {
+    const char* v = getenv(name);
+    return (v != nullptr && atoi(v) == 2) ? 2 : 4;
+}
+int fwd_vec_f32() {
+    static const int v = env_vec("CLB_FWD_VEC");
+    return v;
+}
+int bwd_vec_f32() {
+    static const int v = env_vec("CLB_BWD_VEC");
+    return v;
+}
+
 inline bool aligned(const void* p, int bytes) { return p == nullptr || ((uintptr_t)p % bytes) == 0; }
 
 template <typename T>
@@ -610,10 +628,15 @@ cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* 
     if (gs) g = *gs;
     const bool vec = can_vec<T>(a.ncols, {a.ldx, gs ? gs->ld : ldy}, {a.x, y, gs ? gs->acc : nullptr}) &&
                      (gs == nullptr || (gs->ld % vmax<T>() == 0));
-    const int V = vec ? vmax<T>() : 1;
+    const bool half = vec && std::is_same<T, float>::value && fwd_vec_f32() == 2;
+    const int V = vec ? (half ? 2 : vmax<T>()) : 1;
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-    if (vec) {
+    if (half) {
+        auto k = logic_forward_kernel<T, 2>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
+    } else if (vec) {
         auto k = logic_forward_kernel<T, vmax<T>()>;
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
@@ -669,10 +692,12 @@ cudaError_t bwd_t(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupS
     GroupSumArgs g{};
     if (gs) g = *gs;
     const bool vec = bwd_vec<T>(a, gy, ldgy, gs, gx, ldgx);
-    const int V = vec ? vmax<T>() : 1;
+    const bool half = vec && std::is_same<T, float>::value && bwd_vec_f32() == 2;
+    const int V = vec ? (half ? 2 : vmax<T>()) : 1;
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (part != nullptr && (int64_t)grid.y != part_chunks) return cudaErrorInvalidValue;  // scratch sized for another split
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+    if (half) return bwd_k<T, 2>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
     if (vec) return bwd_k<T, vmax<T>()>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
     return bwd_k<T, 1>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
 }
@@ -730,7 +755,7 @@ int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void*
     bool vec = false;
     int vm = 1;
     switch (dtype) {
-        case CLB_F32: vec = bwd_vec<float>(a, gy, ldgy, gs, gx, ldgx); vm = vmax<float>(); break;
+        case CLB_F32: vec = bwd_vec<float>(a, gy, ldgy, gs, gx, ldgx); vm = bwd_vec_f32(); break;
         case CLB_F64: vec = bwd_vec<double>(a, gy, ldgy, gs, gx, ldgx); vm = vmax<double>(); break;
         case CLB_BF16: vec = bwd_vec<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx); vm = vmax<__nv_bfloat16>(); break;
         default: return -1;

@@ -32,7 +32,7 @@ class PackedLogicNet:
     eval-mode output; predict(x) = argmax (first maximum, as torch.argmax).
     """
 
-    def __init__(self, model: torch.nn.Module, device=None, chunk_words: int = 16):
+    def __init__(self, model: torch.nn.Module, device=None, chunk_words: int = 128):
         mods = list(model)
         if not mods or not isinstance(mods[-1], GroupSum):
             raise ValueError("PackedLogicNet needs a model ending in GroupSum")
