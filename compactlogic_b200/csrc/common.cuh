@@ -30,22 +30,31 @@ template <> __device__ __forceinline__ float from_acc<float>(float v) { return v
 template <> __device__ __forceinline__ __nv_bfloat16 from_acc<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <typename T> __device__ __forceinline__ T from_acc(double v) { return (T)v; }
 
-// VEC consecutive elements as one aligned vector (VEC * sizeof(T) in {4, 8, 16} bytes).
-template <typename T, int VEC> struct alignas(sizeof(T) * VEC) Vec { T v[VEC]; };
+// VEC consecutive elements as one aligned vector of at most 16 bytes.
+template <typename T, int VEC> struct alignas(sizeof(T) * VEC <= 16 ? sizeof(T) * VEC : 16) Vec { T v[VEC]; };
 
+// Vectors wider than 16 bytes are moved as several 16-byte pieces (the pointers are only 16-byte aligned).
 template <typename T, int VEC>
 __device__ __forceinline__ void load_acc(const T* __restrict__ p, typename Acc<T>::type (&out)[VEC]) {
-    Vec<T, VEC> r = *reinterpret_cast<const Vec<T, VEC>*>(p);
+    constexpr int P = (int)(sizeof(T) * VEC <= 16 ? VEC : 16 / sizeof(T));
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) out[i] = to_acc(r.v[i]);
+    for (int o = 0; o < VEC; o += P) {
+        Vec<T, P> r = *reinterpret_cast<const Vec<T, P>*>(p + o);
+#pragma unroll
+        for (int i = 0; i < P; ++i) out[o + i] = to_acc(r.v[i]);
+    }
 }
 
 template <typename T, int VEC>
 __device__ __forceinline__ void store_from_acc(T* __restrict__ p, const typename Acc<T>::type (&in)[VEC]) {
-    Vec<T, VEC> r;
+    constexpr int P = (int)(sizeof(T) * VEC <= 16 ? VEC : 16 / sizeof(T));
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) r.v[i] = from_acc<T>(in[i]);
-    *reinterpret_cast<Vec<T, VEC>*>(p) = r;
+    for (int o = 0; o < VEC; o += P) {
+        Vec<T, P> r;
+#pragma unroll
+        for (int i = 0; i < P; ++i) r.v[i] = from_acc<T>(in[o + i]);
+        *reinterpret_cast<Vec<T, P>*>(p + o) = r;
+    }
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -590,11 +590,12 @@ int choose_tn(size_t bytes_per_neuron) {
 
 template <typename T> constexpr int vmax() { return 16 / (int)sizeof(T); }
 
-// fp32 vector width of the forward / backward column split (4 = 128 columns per CTA, 2 = 64); the
-// environment variables CLB_FWD_VEC / CLB_BWD_VEC select 2 for tuning, read once per process.
+// fp32 vector width of the forward / backward column split (4 = 128 columns per CTA; 2 = 64, 8 = 256);
+// the environment variables CLB_FWD_VEC / CLB_BWD_VEC override it for tuning, read once per process.
 int env_vec(const char* name) {
     const char* v = getenv(name);
-    return (v != nullptr && atoi(v) == 2) ? 2 : 4;
+    const int n = v != nullptr ? atoi(v) : 4;
+    return (n == 2 || n == 8) ? n : 4;
 }
 int fwd_vec_f32() {
     static const int v = env_vec("CLB_FWD_VEC");
@@ -628,11 +629,17 @@ cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* 
     if (gs) g = *gs;
     const bool vec = can_vec<T>(a.ncols, {a.ldx, gs ? gs->ld : ldy}, {a.x, y, gs ? gs->acc : nullptr}) &&
                      (gs == nullptr || (gs->ld % vmax<T>() == 0));
-    const bool half = vec && std::is_same<T, float>::value && fwd_vec_f32() == 2;
-    const int V = vec ? (half ? 2 : vmax<T>()) : 1;
+    const int fv = std::is_same<T, float>::value ? fwd_vec_f32() : vmax<T>();
+    const bool wide = vec && fv == 8 && a.ncols % 8 == 0 && a.ldx % 8 == 0 && (gs ? gs->ld : ldy) % 8 == 0;
+    const bool half = vec && fv == 2;
+    const int V = vec ? (half ? 2 : wide ? 8 : vmax<T>()) : 1;
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-    if (half) {
+    if (wide) {
+        auto k = logic_forward_kernel<T, 8>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
+    } else if (half) {
         auto k = logic_forward_kernel<T, 2>;
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
@@ -682,6 +689,10 @@ bool bwd_vec(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArg
     return true;
 }
 
+inline bool bwd_wide_ok(const LayerArgs& a, int64_t ldgy, const GroupSumArgs* gs, int64_t ldgx) {
+    return a.ncols % 8 == 0 && a.ldx % 8 == 0 && ldgx % 8 == 0 && (gs ? gs->ld : ldgy) % 8 == 0;
+}
+
 template <typename T>
 cudaError_t bwd_t(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs* gs, void* gx, int64_t ldgx,
                   void* part, int64_t part_chunks, cudaStream_t s) {
@@ -692,12 +703,15 @@ cudaError_t bwd_t(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupS
     GroupSumArgs g{};
     if (gs) g = *gs;
     const bool vec = bwd_vec<T>(a, gy, ldgy, gs, gx, ldgx);
-    const bool half = vec && std::is_same<T, float>::value && bwd_vec_f32() == 2;
-    const int V = vec ? (half ? 2 : vmax<T>()) : 1;
+    const int bv = std::is_same<T, float>::value ? bwd_vec_f32() : vmax<T>();
+    const bool wide = vec && bv == 8 && bwd_wide_ok(a, ldgy, gs, ldgx);
+    const bool half = vec && bv == 2;
+    const int V = vec ? (half ? 2 : wide ? 8 : vmax<T>()) : 1;
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (part != nullptr && (int64_t)grid.y != part_chunks) return cudaErrorInvalidValue;  // scratch sized for another split
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
     if (half) return bwd_k<T, 2>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
+    if (wide) return bwd_k<T, 8>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
     if (vec) return bwd_k<T, vmax<T>()>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
     return bwd_k<T, 1>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
 }
@@ -755,7 +769,11 @@ int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void*
     bool vec = false;
     int vm = 1;
     switch (dtype) {
-        case CLB_F32: vec = bwd_vec<float>(a, gy, ldgy, gs, gx, ldgx); vm = bwd_vec_f32(); break;
+        case CLB_F32:
+            vec = bwd_vec<float>(a, gy, ldgy, gs, gx, ldgx);
+            vm = bwd_vec_f32();
+            if (vm == 8 && !bwd_wide_ok(a, gs ? 0 : ldgy, gs, ldgx)) vm = 4;
+            break;
         case CLB_F64: vec = bwd_vec<double>(a, gy, ldgy, gs, gx, ldgx); vm = vmax<double>(); break;
         case CLB_BF16: vec = bwd_vec<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx); vm = vmax<__nv_bfloat16>(); break;
         default: return -1;
