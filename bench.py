@@ -220,6 +220,60 @@ def bench_c2(args, dev, rank, world):
     return res, model
 
 
+def bench_c2_reference_kernels(args, dev):
+    """The same c2 step driven through the reference's own CUDA kernels (oracle/_ref, built unmodified
+    for sm_100) with the reference's Python around them: softmax in torch (compactlogic.py:108), the
+    three kernels through the autograd bridge (compactlogic.py:474-508), GroupSum in torch
+    (compactlogic.py:460-465).  Reported beside the native step; not part of the product."""
+    import importlib.util
+    path = os.path.join(ROOT, "oracle", "_ref", "difflogic_cuda.so")
+    if not os.path.exists(path):
+        return {"unavailable": "oracle/_ref/difflogic_cuda.so not built (needs the reference tree at build time)"}
+    spec = importlib.util.spec_from_file_location("difflogic_cuda", path)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+
+    class RefFn(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, x, a, b, w, g, st, ys, codes):
+            ctx.save_for_backward(x, a, b, w, g, st, ys, codes)
+            return ref.forward(x, a, b, w, g)
+
+        @staticmethod
+        def backward(ctx, gy):
+            x, a, b, w, g, st, ys, codes = ctx.saved_tensors
+            gy = gy.contiguous()
+            gx = ref.backward_x(x, a, b, w, g, gy, st, ys, codes) if ctx.needs_input_grad[0] else None
+            gw = ref.backward_w(x, a, b, g, gy) if ctx.needs_input_grad[3] else None
+            return gx, None, None, gw, None, None, None, None
+
+    model = build_c2(dev)
+    layers = [m for m in model if hasattr(m, "indices")]
+    params = [m.weights for m in layers]
+    opt = torch.optim.Adam(params, lr=0.01, fused=True)
+    x_host, y_host = c2_inputs(1000, C2["batch"])
+    x_dev, y_dev = x_host.to(dev), y_host.to(dev)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        h = x_dev
+        for m in layers:
+            xt = h.transpose(0, 1).contiguous()
+            w = torch.nn.functional.softmax(m.weights, dim=-1).to(xt.dtype)
+            h = RefFn.apply(xt, m.indices[0], m.indices[1], w, m.gate_sequence, m.given_x_indices_of_y_start,
+                            m.given_x_indices_of_y, m.given_x_indices_of_gate).transpose(0, 1)
+        logits = h.reshape(h.shape[0], C2["k"], -1).sum(-1) / C2["tau"]
+        loss = torch.nn.functional.cross_entropy(logits, y_dev)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(params, 10.0)
+        opt.step()
+
+    steps = max(2, args.steps // 3)
+    ms = timed(step, steps, 2, dev)
+    return {"value": round(C2["batch"] / (ms / 1e3), 1), "unit": "samples/s", "ms_per_step": round(ms, 3),
+            "steps": steps, "what": "same c2 step on the reference CUDA kernels compiled for sm_100"}
+
+
 def cpu_baseline_c2(model, budget_s):
     """The oracle (reference kernels restated in C, all host threads) on a bounded sub-batch of the
     c2 step: forward through the 6 layers, GroupSum + CE gradient, backward (grad_x and grad_w)."""
@@ -361,6 +415,7 @@ def main():
     ap.add_argument("--workload", default="c2", choices=["c2", "c4"])
     ap.add_argument("--no-packed", action="store_true", help="skip the packed-inference (c4) sub-measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-refcuda", action="store_true", help="skip the reference-CUDA-kernel step timing")
     ap.add_argument("--chunk-words", type=int, default=128)
     ap.add_argument("--layers", type=int, default=None, help="override the c2 depth (profiling on a smaller case)")
     ap.add_argument("--samples", type=int, default=None, help="override the c4 sample count (profiling)")
@@ -417,6 +472,9 @@ def main():
                 packed["cpu_baseline"] = cpu_baseline_c4(pmodel, args.cpu_budget / 2)
             res["packed"] = packed
             del pmodel
+        if world == 1 and not args.no_refcuda:
+            res["reference_cuda_kernels"] = bench_c2_reference_kernels(args, dev)
+            torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu:
             res["cpu_baseline"] = cpu_baseline_c2(build_c2("cpu"), args.cpu_budget)
     if rank == 0:
