@@ -155,3 +155,41 @@ def test_packed_layer_fast_equals_bitwise():
     ab = rng.integers(-1, 50, (70, 2)).astype(np.int32)
     gate = rng.integers(0, 16, 70)
     np.testing.assert_array_equal(O.packed_layer(xw, ab, gate), O.packed_layer(xw, ab, gate, fast=True))
+
+
+def test_oracle_matches_reference_cuda_kernels(golden):
+    """The oracle reproduces the outputs of the reference's own CUDA extensions (run on a B200 by
+    tests/golden/make_golden_gpu.py): dense forward / backward_w / backward_x (CSR and atomic) / eval,
+    packbits / groupbitsum at every word width, conv forward / backward_x / backward_w / eval."""
+    d = golden("ref_cuda.npz")
+    x, a, b, w, g, gy = (d[k] for k in ("dense_x", "dense_a", "dense_b", "dense_w", "dense_g", "dense_gy"))
+    # The fixture ran the reference in fp64, but its gate polynomial goes through fmaf with float
+    # coefficients (compactlogic/cuda/utils.cuh:189-195) and its derivatives are computed in float
+    # (utils.cuh:219-241), and backward_w sums in float (difflogic_kernel.cu:92-110): its fp64 results
+    # carry float rounding, so compare at 1e-6 relative to the largest magnitude of each output.
+    def close(got, ref, rtol=1e-6):
+        np.testing.assert_allclose(got, ref, rtol=rtol, atol=rtol * np.abs(ref).max())
+
+    close(O.dense_forward(x, a, b, w, g), d["dense_y"])
+    close(O.dense_forward(x, a, b, w, g), d["dense_y_f32"], 1e-5)
+    close(O.dense_backward_w(x, a, b, g, gy), d["dense_gw"])
+    starts, ys, codes = O.inverse_index(a, b, x.shape[0])
+    for name, ref in (("starts", starts), ("ys", ys), ("codes", codes)):
+        np.testing.assert_array_equal(ref, d[f"dense_{name}"])
+    close(O.dense_backward_x_csr(x, a, b, w, g, gy, starts, ys, codes), d["dense_gx"])
+    close(O.dense_backward_x(x, a, b, w, g, gy), d["dense_gx_atomic"])
+    np.testing.assert_array_equal(O.dense_eval(d["dense_xb"], a, b, d["dense_sel"], g), d["dense_eval"])
+    t = d["pack_t"].astype(bool)
+    for bits in (8, 16, 32, 64):
+        words, pad = O.packbits(t, bits)
+        np.testing.assert_array_equal(words, d[f"pack_words_{bits}"])
+        assert pad == int(d[f"pack_pad_{bits}"])
+        np.testing.assert_array_equal(O.groupbitsum(words, pad, 5), d[f"groupbitsum_{bits}"])
+    stride, pad, ks = (int(v) for v in d["conv_meta"])
+    cx, och, oh, ow, cw, cg, cgy = (d[k] for k in ("conv_x", "conv_och", "conv_oh", "conv_ow", "conv_w", "conv_g",
+                                                     "conv_gy"))
+    close(O.conv_forward(cx, och, oh, ow, cw, cg, stride, pad, ks), d["conv_y"])
+    close(O.conv_backward_x(cx, och, oh, ow, cw, cg, cgy, stride), d["conv_gx"])
+    close(O.conv_backward_w(cx, och, oh, ow, cg, cgy, stride), d["conv_gw"])
+    np.testing.assert_array_equal(O.conv_eval(d["conv_xb"], och, oh, ow, d["conv_sel"], cg, stride, pad, ks),
+                                  d["conv_eval"])
