@@ -33,6 +33,8 @@ sys.path.insert(0, ROOT)
 
 C2 = dict(in_dim=784, width=64000, layers=6, K=16, k=10, tau=10.0, batch=1024)
 C4 = dict(in_dim=784, width=256000, layers=8, k=10, tau=1.0, samples=1 << 22)
+C3 = dict(batch=512, K=16, dense=128000, k=10, tau=20.0)
+C5 = dict(in_dim=3072, width=1_000_000, layers=4, K=4, k=100, tau=30.0, batch=512)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -274,6 +276,91 @@ def bench_c2_reference_kernels(args, dev):
             "steps": steps, "what": "same c2 step on the reference CUDA kernels compiled for sm_100"}
 
 
+# ------------------------------------------------------------------------------------------------
+# c3: conv model training step;  c5: wide compact-gate bf16 training step
+# ------------------------------------------------------------------------------------------------
+def build_c3(dev):
+    import compactlogic_b200 as cl
+    torch.manual_seed(1)
+    conv1 = cl.ConvLayer((9, 32, 32), 1, 128, 3, 2, num_gates=C3["K"])
+    conv2 = cl.ConvLayer((128, 16, 16), 1, 256, 3, 2, num_gates=C3["K"])
+    dense = cl.LogicLayer(256 * 8 * 8, C3["dense"], num_gates=C3["K"])
+    model = torch.nn.Sequential(conv1, conv2, torch.nn.Flatten(), dense, cl.GroupSum(C3["k"], C3["tau"])).to(dev)
+    return cl.fuse_groupsum(model)
+
+
+def c3_inputs(seed, batch):
+    """3 channels of U(0,1) pixels thresholded at 1/4, 2/4, 3/4 (experiments/experiment_script.py:92)."""
+    g = torch.Generator().manual_seed(seed)
+    px = torch.rand(batch, 3, 1, 32, 32, generator=g)
+    thr = torch.tensor([0.25, 0.5, 0.75]).view(1, 1, 3, 1, 1)
+    x = (px > thr).float().reshape(batch, 9, 32, 32)
+    return x, torch.randint(0, C3["k"], (batch,), generator=g)
+
+
+def build_c5(dev):
+    import compactlogic_b200 as cl
+    torch.manual_seed(5)
+    widths = [C5["in_dim"]] + [C5["width"]] * C5["layers"]
+    layers = []
+    for i in range(C5["layers"]):
+        layer = cl.LogicLayer(widths[i], widths[i + 1], num_gates=C5["K"])
+        with torch.no_grad():  # candidate gate ids uniform in [0, 16) instead of the constructor's 0..K-1
+            layer.gate_sequence.copy_(torch.randint(0, 16, layer.gate_sequence.shape, dtype=torch.uint8))
+        layers.append(layer)
+    model = torch.nn.Sequential(*layers, cl.GroupSum(C5["k"], C5["tau"])).to(dev)
+    return cl.fuse_groupsum(model)
+
+
+def c5_inputs(seed, batch):
+    g = torch.Generator().manual_seed(seed)
+    return ((torch.rand(batch, C5["in_dim"], generator=g) < 0.5).to(torch.bfloat16),
+            torch.randint(0, C5["k"], (batch,), generator=g))
+
+
+def bench_train(args, dev, rank, world, workload):
+    """Training step of c3 / c5 (same loop and timing rules as c2)."""
+    from compactlogic_b200.parallel import GradAllReduce
+    if workload == "c3":
+        model, (x_host, y_host), B, dtype = build_c3(dev), c3_inputs(1000 + rank, C3["batch"]), C3["batch"], "f32"
+        desc = "c3: (9,32,32) -> Conv(128,ks3,s2,p1) -> Conv(256,ks3,s2,p1) -> LogicLayer(128000) -> GroupSum(10, 20)"
+    else:
+        model, (x_host, y_host), B, dtype = build_c5(dev), c5_inputs(1000 + rank, C5["batch"]), C5["batch"], "bf16"
+        desc = "c5: 3072 -> 4x LogicLayer(1e6, K=4, gate ids U{0..15}) -> GroupSum(100, 30); bf16 activations"
+    params = [p for p in model.parameters() if p.requires_grad]
+    opt = torch.optim.Adam(params, lr=0.01, fused=True)
+    sync = GradAllReduce(params)
+    x_dev, y_dev = x_host.to(dev), y_host.to(dev)
+
+    def step(x, y):
+        opt.zero_grad(set_to_none=True)
+        loss = torch.nn.functional.cross_entropy(model(x), y)
+        loss.backward()
+        sync.finish()
+        torch.nn.utils.clip_grad_norm_(params, 10.0)
+        opt.step()
+        return loss
+
+    with Clocks(dev.index) as clk:
+        ms = timed(lambda: step(x_dev, y_dev), args.steps, args.warmup, dev)
+    xp, yp = x_host.pin_memory(), y_host.pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def e2e():
+        loss = step(xp.to(dev, non_blocking=True), yp.to(dev, non_blocking=True))
+        loss_host.copy_(loss.detach(), non_blocking=True)
+
+    ms_e2e = timed(e2e, args.steps, 1, dev)
+    return {"metric": "train_samples_per_s", "value": round(world * B / (ms / 1e3), 1), "unit": "samples/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "config": {"workload": desc, "batch_per_gpu": B, "global_batch": B * world, "parallelism": f"dp{world}"},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(world * B / (ms_e2e / 1e3), 1), "unit": "samples/s",
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size() + y_host.numel() * 8,
+                    "d2h_bytes_per_step": 4}}
+
+
 def cpu_baseline_c2(model, budget_s):
     """The oracle (reference kernels restated in C, all host threads) on a bounded sub-batch of the
     c2 step: forward through the 6 layers, GroupSum + CE gradient, backward (grad_x and grad_w)."""
@@ -412,7 +499,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"])
     ap.add_argument("--no-packed", action="store_true", help="skip the packed-inference (c4) sub-measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-refcuda", action="store_true", help="skip the reference-CUDA-kernel step timing")
@@ -456,7 +543,9 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
 
-    if args.workload == "c4":
+    if args.workload in ("c3", "c5"):
+        res = bench_train(args, dev, rank, world, args.workload)
+    elif args.workload == "c4":
         res, model = bench_c4(args, dev, rank, world, args.chunk_words)
         if rank == 0 and world == 1 and not args.no_cpu:
             res["cpu_baseline"] = cpu_baseline_c4(model, args.cpu_budget)

@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
-from .functional import LayerSpec, LogicGroupSumFn, LogicLayerFn, eval_forward, eval_group_sum
+from .functional import GradSlot, LayerSpec, LogicGroupSumFn, LogicLayerFn, eval_forward, eval_group_sum
 
 __all__ = [
     "LogicLayer", "GroupSum", "LogicLayerCudaFunction", "ConvLayer", "ConvLayerCudaFunction",
@@ -83,14 +83,19 @@ class LogicLayer(torch.nn.Module):
 
     def forward_cuda(self, x):
         """Train-mode forward (compactlogic.py:83-118): softmax + gate mix in one kernel."""
+        in_slot = getattr(x, "_clb_slot", None)
         xt = self._to_feature_major(x)
         spec = self._layer_spec(xt.device)
         w = self._weights_for(xt.dtype)
         if self._fused_groupsum is not None:
             k, tau = self._fused_groupsum
-            acc = LogicGroupSumFn.apply(xt, w, spec, k, _group_size(self.out_dim, k))
+            acc = LogicGroupSumFn.apply(xt, w, spec, k, _group_size(self.out_dim, k), in_slot)
             return acc.transpose(0, 1) / tau
-        return LogicLayerFn.apply(xt, w, spec).transpose(0, 1)
+        out_slot = GradSlot() if xt.dtype == torch.bfloat16 else None
+        y = LogicLayerFn.apply(xt, w, spec, in_slot, out_slot).transpose(0, 1)
+        if out_slot is not None:
+            y._clb_slot = out_slot
+        return y
 
     @torch.no_grad()
     def forward_cuda_eval(self, x):
@@ -454,9 +459,14 @@ class ConvLayer(LogicLayer):
         """Train-mode conv forward (compactlogic.py:598-626)."""
         if self.training:
             assert x.device.type == 'cuda', x.device
+        in_slot = getattr(x, "_clb_slot", None)
         xt = self._to_feature_major(x)
         spec = self._layer_spec(xt.device)
-        return self._to_public(LogicLayerFn.apply(xt, self._weights_for(xt.dtype), spec))
+        out_slot = GradSlot() if xt.dtype == torch.bfloat16 else None
+        y = self._to_public(LogicLayerFn.apply(xt, self._weights_for(xt.dtype), spec, in_slot, out_slot))
+        if out_slot is not None:
+            y._clb_slot = out_slot
+        return y
 
     @torch.no_grad()
     def forward_cuda_eval(self, x):

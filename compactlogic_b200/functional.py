@@ -123,31 +123,66 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
     return gx, gw
 
 
+class GradSlot:
+    """fp32 gradient hand-over between two logic layers whose activations are low precision (bf16).
+
+    Autograd casts a gradient to the dtype of the tensor it belongs to, which would round every
+    inter-layer gradient to bf16.  A producing layer attaches a slot to its output; a logic layer that
+    consumes that output deposits its fp32 grad_x in the slot and hands autograd a zero-stride
+    placeholder instead; the producer's backward adds the slot's fp32 gradient to whatever autograd
+    delivers (other consumers' contributions, if any).  fp32 and fp64 activations do not use slots."""
+    __slots__ = ("grad",)
+
+    def __init__(self):
+        self.grad = None
+
+    def add(self, g):
+        self.grad = g if self.grad is None else self.grad + g
+
+
+def _placeholder(g: torch.Tensor) -> bool:
+    return all(s == 0 for s in g.stride())
+
+
+def _incoming_grad(gy: torch.Tensor, slot, acc_dtype) -> torch.Tensor:
+    if slot is not None and slot.grad is not None:
+        g, slot.grad = slot.grad, None
+        return g if _placeholder(gy) else g + gy.to(acc_dtype)
+    return gy.to(acc_dtype)
+
+
+def _outgoing_grad(gx, xt: torch.Tensor, in_slot):
+    if gx is not None and in_slot is not None:
+        in_slot.add(gx)
+        return torch.zeros((), dtype=xt.dtype, device=xt.device).expand(xt.shape)
+    return gx
+
+
 class LogicLayerFn(torch.autograd.Function):
     """y [n_out, B] = soft logic layer of xt [in, B] with gate logits `weights` [rows, K].
 
     Fuses the reference's ``softmax(weights)`` (compactlogic/compactlogic.py:108), the kernel
     forward (difflogic_kernel.cu:39-78) and, in backward, grad_x, grad_w and the softmax backward
-    (compactlogic.py:488-508 + torch autograd)."""
+    (compactlogic.py:488-508 + torch autograd).  in_slot / out_slot: see GradSlot."""
 
     @staticmethod
-    def forward(ctx, xt, weights, spec: LayerSpec):
+    def forward(ctx, xt, weights, spec: LayerSpec, in_slot=None, out_slot=None):
         y = torch.empty(spec.n_out, xt.shape[1], dtype=xt.dtype, device=xt.device)
         forward_into(xt, weights, spec, L.W_LOGITS, y=y)
         ctx.save_for_backward(xt, weights)
-        ctx.spec = spec
+        ctx.spec, ctx.in_slot, ctx.out_slot = spec, in_slot, out_slot
         return y
 
     @staticmethod
     def backward(ctx, gy):
         xt, weights = ctx.saved_tensors
         spec = ctx.spec
-        gy = gy.to(L.acc_dtype(xt.dtype))
+        gy = _incoming_grad(gy, ctx.out_slot, L.acc_dtype(xt.dtype))
         if gy.stride(1) != 1 or gy.stride(0) < gy.shape[1]:
             gy = gy.contiguous()
         gx, gw = backward_into(xt, weights, spec, L.W_LOGITS, gy, None, 0, 1.0, ctx.needs_input_grad[0],
                                ctx.needs_input_grad[1])
-        return gx, gw, None
+        return _outgoing_grad(gx, xt, ctx.in_slot), gw, None, None, None
 
 
 class LogicGroupSumFn(torch.autograd.Function):
@@ -156,11 +191,11 @@ class LogicGroupSumFn(torch.autograd.Function):
     synthesises grad_y[j, n] = grad[class(j), n] on the fly."""
 
     @staticmethod
-    def forward(ctx, xt, weights, spec: LayerSpec, k: int, gs_size: int):
+    def forward(ctx, xt, weights, spec: LayerSpec, k: int, gs_size: int, in_slot=None):
         acc = torch.zeros(k, xt.shape[1], dtype=L.acc_dtype(xt.dtype), device=xt.device)
         forward_into(xt, weights, spec, L.W_LOGITS, gs_acc=acc, gs_size=gs_size)
         ctx.save_for_backward(xt, weights)
-        ctx.spec, ctx.gs_size = spec, gs_size
+        ctx.spec, ctx.gs_size, ctx.in_slot = spec, gs_size, in_slot
         return acc
 
     @staticmethod
@@ -169,7 +204,7 @@ class LogicGroupSumFn(torch.autograd.Function):
         gacc = gacc.contiguous().to(L.acc_dtype(xt.dtype))
         gx, gw = backward_into(xt, weights, ctx.spec, L.W_LOGITS, None, gacc, ctx.gs_size, 1.0,
                                ctx.needs_input_grad[0], ctx.needs_input_grad[1])
-        return gx, gw, None, None, None
+        return _outgoing_grad(gx, xt, ctx.in_slot), gw, None, None, None, None
 
 
 def eval_forward(xt: torch.Tensor, spec: LayerSpec, select: torch.Tensor) -> torch.Tensor:

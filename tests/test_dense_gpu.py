@@ -161,3 +161,33 @@ def test_frozen_layer_runs_eval_in_train_mode():
     idx = layer.indices.cpu().numpy()
     ref = O.dense_eval(x.cpu().numpy().T, idx[0], idx[1], layer.w.cpu().numpy(), layer.gate_sequence.cpu().numpy()).T
     np.testing.assert_array_equal(layer(x).cpu().numpy(), ref)
+
+
+def _bf16(a):
+    return torch.from_numpy(np.asarray(a, np.float32)).bfloat16().double().numpy()
+
+
+def test_bf16_chain_keeps_fp32_gradients():
+    """bf16 activations, fp32 logits and gradients (BASELINE config c5 regime): a 3-layer chain with
+    fused GroupSum against the oracle run on the bf16-rounded activations, 1e-2 relative."""
+    torch.manual_seed(3)
+    layers = [cl.LogicLayer(96, 256, num_gates=4), cl.LogicLayer(256, 256, num_gates=4), cl.LogicLayer(256, 200, num_gates=4)]
+    model = cl.fuse_groupsum(torch.nn.Sequential(*layers, cl.GroupSum(10, 3.0))).cuda()
+    x = (torch.rand(64, 96) < 0.5).float()
+    labels = torch.randint(0, 10, (64,))
+    logits = model(x.cuda().bfloat16())
+    torch.nn.functional.cross_entropy(logits, labels.cuda()).backward()
+    tabs = [(m.indices.cpu().numpy(), m.gate_sequence.cpu().numpy(), O.softmax(m.weights.detach().cpu().numpy()))
+            for m in layers]
+    h = [x.numpy().T.astype(np.float64)]
+    for li, (idx, g, p) in enumerate(tabs):
+        y = O.dense_forward(h[-1], idx[0], idx[1], p, g)
+        h.append(_bf16(y) if li < len(tabs) - 1 else y)
+    ref_logits = O.group_sum(h[-1].T, 10, 3.0)
+    assert_close(logits, ref_logits, 1e-2, "bf16 logits")
+    gy = O.group_sum_backward(O.cross_entropy_grad(ref_logits, labels.numpy()), 200, 10, 3.0).T
+    for li in range(len(tabs) - 1, -1, -1):
+        idx, g, p = tabs[li]
+        gw = O.softmax_backward(p, O.dense_backward_w(h[li], idx[0], idx[1], g, gy))
+        assert_close(layers[li].weights.grad, gw, 1e-2, f"bf16 grad layer {li}")
+        gy = O.dense_backward_x(h[li], idx[0], idx[1], p, g, gy)
