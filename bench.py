@@ -32,6 +32,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 C2 = dict(in_dim=784, width=64000, layers=6, K=16, k=10, tau=10.0, batch=1024)
+
+# DRAM bytes (read + write) per launch of the dominant c2 kernel from one ncu capture
+# (profiles/logic_layer_kernels_c2.md): 2.092 GB for a 64000->64000 layer with grad_x, 0.320 GB for the
+# 784->64000 first layer; averaged over the 6 backward launches of a step.  Cold-cache (ncu flushes
+# before each pass), so an upper bound of the steady state.
+NCU_TRAFFIC = {"logic_backward_kernel": (5 * 2.092e9 + 0.320e9) / 6}
 C4 = dict(in_dim=784, width=256000, layers=8, k=10, tau=1.0, samples=1 << 22)
 C3 = dict(batch=512, K=16, dense=128000, k=10, tau=20.0)
 C5 = dict(in_dim=3072, width=1_000_000, layers=4, K=4, k=100, tau=30.0, batch=512)
@@ -199,7 +205,9 @@ def bench_c2(args, dev, rank, world):
         achieved = tot_b / (tot_ms / 1e3) / 1e9
         roof = {"kernel": f"logic_{dom}_kernel", "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                 "peak_source": src, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                "traffic": None, "launches": n, "avg_ms": round(tot_ms / n, 4),
+                "traffic": NCU_TRAFFIC.get(f"logic_{dom}_kernel") if C2["layers"] == 6 else None,
+                "traffic_note": "ncu dram__bytes_read+write per launch, cold cache (profiles/)",
+                "algorithmic_bytes_per_launch": round(tot_b / n), "launches": n, "avg_ms": round(tot_ms / n, 4),
                 "shares": {k: round(v[1] / sum(w[1] for w in kern.values()), 3) for k, v in kern.items()}}
     step_bytes = c2_bytes_per_step(B)
     res = {
