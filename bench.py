@@ -369,7 +369,7 @@ def bench_train(args, dev, rank, world, workload):
                     "d2h_bytes_per_step": 4}}
 
 
-def cpu_baseline_c2(model, budget_s):
+def cpu_baseline_c2(model, budget_s, steps=1):
     """The oracle (reference kernels restated in C, all host threads) on a bounded sub-batch of the
     c2 step: forward through the 6 layers, GroupSum + CE gradient, backward (grad_x and grad_w)."""
     from oracle import oracle as O
@@ -396,8 +396,9 @@ def cpu_baseline_c2(model, budget_s):
     b = int(max(4, min(1024, 4 * budget_s / max(t4, 1e-3))))
     b = max(4, (b // 4) * 4)
     t = time.perf_counter()
-    run(b)
-    dt = time.perf_counter() - t
+    for _ in range(steps):
+        run(b)
+    dt = (time.perf_counter() - t) / steps
     return {"value": round(b / dt, 3), "unit": "samples/s", "cores": O.THREADS, "kind": "port",
             "sample": f"one c2 training step (fwd+bwd of 6 layers, no optimizer) on a sub-batch of {b} samples, "
                       f"{dt:.1f} s"}
@@ -475,7 +476,7 @@ def bench_c4(args, dev, rank, world, chunk_words):
     }, model
 
 
-def cpu_baseline_c4(model, budget_s):
+def cpu_baseline_c4(model, budget_s, steps=1):
     from oracle import oracle as O
     layers = [m for m in model if hasattr(m, "indices")]
     tabs = [O.frozen_tables(m.indices.cpu().numpy(), m.gate_sequence.cpu().numpy(), m.w.cpu().numpy())
@@ -493,8 +494,9 @@ def cpu_baseline_c4(model, budget_s):
     t1 = time.perf_counter() - t
     words = int(max(1, min(4096, budget_s / max(t1, 1e-3))))
     t = time.perf_counter()
-    run(words)
-    dt = time.perf_counter() - t
+    for _ in range(steps):
+        run(words)
+    dt = (time.perf_counter() - t) / steps
     evals = 64 * words * C4["width"] * C4["layers"]
     return {"value": round(evals / dt, 1), "unit": "gate-evals/s", "cores": O.THREADS, "kind": "port",
             "sample": f"{64 * words} samples through all 8 layers + counts (uint64 word loop), {dt:.1f} s"}
@@ -531,14 +533,15 @@ def main():
         if rank != 0:
             return
         torch.manual_seed(0)
+        per_step = max(1.0, min(args.cpu_budget, 150.0 / max(1, args.steps)))  # whole arm within a few minutes
         if args.workload == "c4":
-            res = cpu_baseline_c4(build_c4("cpu"), args.cpu_budget)
+            res = cpu_baseline_c4(build_c4("cpu"), per_step, args.steps)
             metric = "packed_infer_gate_evals_per_s"
         else:
-            res = cpu_baseline_c2(build_c2("cpu"), args.cpu_budget)
+            res = cpu_baseline_c2(build_c2("cpu"), per_step, args.steps)
             metric = "train_samples_per_s"
         line = {"impl": "reference", "metric": metric, "value": res["value"], "unit": res["unit"], "n_gpus": world,
-                "steps": 1, "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "steps": args.steps, "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f64" if metric.startswith("train") else "u64", "data": "synthetic",
                 "config": {"workload": args.workload, "arm": "CPU oracle (reference kernels restated in C)"},
                 "cpu_baseline": res,
