@@ -300,9 +300,8 @@ def build_c3(dev):
 def c3_inputs(seed, batch):
     """3 channels of U(0,1) pixels thresholded at 1/4, 2/4, 3/4 (experiments/experiment_script.py:92)."""
     g = torch.Generator().manual_seed(seed)
-    px = torch.rand(batch, 3, 1, 32, 32, generator=g)
-    thr = torch.tensor([0.25, 0.5, 0.75]).view(1, 1, 3, 1, 1)
-    x = (px > thr).float().reshape(batch, 9, 32, 32)
+    px = torch.rand(batch, 3, 32, 32, generator=g)
+    x = torch.cat([(px > (i + 1) / 4).float() for i in range(3)], dim=1)  # threshold-major channels
     return x, torch.randint(0, C3["k"], (batch,), generator=g)
 
 

@@ -5,6 +5,6 @@ LogicLayer / ConvLayer / GroupSum / hooks API (compactlogic/__init__.py:1).
 """
 from .compactlogic import *  # noqa: F401,F403
 from .compactlogic import __all__ as _api
-from .packed import PackedLogicNet  # noqa: F401
+from .packed import PackedLogicNet, packed_from_state_dict  # noqa: F401
 
-__all__ = list(_api) + ["PackedLogicNet"]
+__all__ = list(_api) + ["PackedLogicNet", "packed_from_state_dict"]

@@ -229,6 +229,16 @@ int clb_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, i
     return cuda_status(launch_pack_inputs(dtype, x, batch, features, ldx, out, ldw, S(stream)), "pack_inputs");
 }
 
+int clb_pack_thresholds(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, int nthr,
+                        uint64_t* out, int64_t ldw, clb_stream_t stream) {
+    if (!dtype_ok(dtype)) return fail(CLB_ERR_DTYPE, "pack_thresholds: dtype");
+    if (batch < 0 || features < 0 || ldx < features || nthr < 1 || nthr > 64 || ldw < (batch + 63) / 64)
+        return fail(CLB_ERR_INVALID, "pack_thresholds: bad sizes");
+    if (batch * features > 0 && (!x || !out)) return fail(CLB_ERR_INVALID, "pack_thresholds: null");
+    return cuda_status(launch_pack_thresholds(dtype, x, batch, features, ldx, nthr, out, ldw, S(stream)),
+                       "pack_thresholds");
+}
+
 int clb_packed_select(const int32_t* slots, const uint8_t* gates, const uint8_t* select, int64_t n_out, int64_t K,
                       int64_t group, int32_t* sel_ab, uint8_t* sel_gate, clb_stream_t stream) {
     if (n_out < 0 || K < 1 || K > 256 || group < 1 || n_out % group) return fail(CLB_ERR_INVALID, "packed_select: sizes");

@@ -80,6 +80,8 @@ cudaError_t launch_groupbitsum(const uint8_t* words, int64_t rows, int64_t row_b
                                cudaStream_t s);
 cudaError_t launch_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx,
                                uint64_t* out, int64_t ldw, cudaStream_t s);
+cudaError_t launch_pack_thresholds(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, int nthr,
+                                   uint64_t* out, int64_t ldw, cudaStream_t s);
 cudaError_t launch_packed_select(const int32_t* slots, const uint8_t* gates, const uint8_t* select, int64_t n_out,
                                  int K, int64_t group, int32_t* sel_ab, uint8_t* sel_gate, cudaStream_t s);
 cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,

@@ -141,6 +141,29 @@ __global__ void pack_inputs_kernel(const T* __restrict__ x, int64_t batch, int64
     }
 }
 
+// pack_thresholds: raw inputs x [batch, C*HW] -> nthr*C*HW packed features, feature t*C*HW + f having
+// bit = x[s, f] > (t+1)/(nthr+1) (the reference's CIFAR binarisation, experiments/experiment_script.py:92,
+// threshold-major channel order).  Each raw value is read once for all thresholds.
+template <typename T>
+__global__ void pack_thresholds_kernel(const T* __restrict__ x, int64_t batch, int64_t features, int64_t ldx,
+                                       int nthr, uint64_t* __restrict__ out, int64_t ldw) {
+    __shared__ float tile[64][33];
+    const int64_t s0 = (int64_t)blockIdx.y * 64, f0 = (int64_t)blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 64; i += blockDim.y) {
+        const int64_t s = s0 + i, f = f0 + threadIdx.x;
+        tile[i][threadIdx.x] = (s < batch && f < features) ? (float)to_acc(x[s * ldx + f]) : -1.0f;
+    }
+    __syncthreads();
+    const int64_t f = f0 + threadIdx.x;
+    for (int t = threadIdx.y; t < 2 * nthr; t += blockDim.y) {  // (threshold, 32-sample half) pairs
+        const int thr = t >> 1, half = t & 1;
+        const float level = (float)((thr + 1.0) / (nthr + 1.0));
+        uint32_t bits = 0;
+        for (int i = 0; i < 32; ++i) bits |= (uint32_t)(tile[half * 32 + i][threadIdx.x] > level) << i;
+        if (f < features) reinterpret_cast<uint32_t*>(out + ((int64_t)thr * features + f) * ldw + blockIdx.y)[half] = bits;
+    }
+}
+
 __global__ void packed_select_kernel(const int2* __restrict__ slots, const uint8_t* __restrict__ gates,
                                      const uint8_t* __restrict__ select, int64_t n_out, int K, int64_t group,
                                      int2* __restrict__ sel_ab, uint8_t* __restrict__ sel_gate) {
@@ -424,6 +447,20 @@ cudaError_t launch_pack_inputs(int dtype, const void* x, int64_t batch, int64_t 
         case CLB_F32: pack_inputs_kernel<float><<<grid, block, 0, s>>>((const float*)x, batch, features, ldx, out, ldw); break;
         case CLB_F64: pack_inputs_kernel<double><<<grid, block, 0, s>>>((const double*)x, batch, features, ldx, out, ldw); break;
         case CLB_BF16: pack_inputs_kernel<__nv_bfloat16><<<grid, block, 0, s>>>((const __nv_bfloat16*)x, batch, features, ldx, out, ldw); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_thresholds(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, int nthr,
+                                   uint64_t* out, int64_t ldw, cudaStream_t s) {
+    if (batch == 0 || features == 0) return cudaSuccess;
+    dim3 grid((unsigned)ceil_div64(features, 32), (unsigned)ceil_div64(batch, 64));
+    dim3 block(32, 8);
+    switch (dtype) {
+        case CLB_F32: pack_thresholds_kernel<float><<<grid, block, 0, s>>>((const float*)x, batch, features, ldx, nthr, out, ldw); break;
+        case CLB_F64: pack_thresholds_kernel<double><<<grid, block, 0, s>>>((const double*)x, batch, features, ldx, nthr, out, ldw); break;
+        case CLB_BF16: pack_thresholds_kernel<__nv_bfloat16><<<grid, block, 0, s>>>((const __nv_bfloat16*)x, batch, features, ldx, nthr, out, ldw); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

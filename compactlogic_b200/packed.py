@@ -91,6 +91,29 @@ class PackedLogicNet:
                L.stream(self.device))
         return xw
 
+    def pack_raw(self, x: torch.Tensor, nthr: int) -> torch.Tensor:
+        """Raw inputs [batch, C, H, W] (or [batch, F]) in [0, 1] -> [nthr*F, W] packed words, thresholding at
+        (i+1)/(nthr+1) in the reference's order (experiments/experiment_script.py:92) in the same pass."""
+        x = x.reshape(x.shape[0], -1)
+        if x.dtype not in (torch.float32, torch.float64, torch.bfloat16):
+            x = x.to(torch.float32)
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        B, F = x.shape
+        if F * nthr != self.in_features:
+            raise ValueError(f"{F} raw features x {nthr} thresholds != {self.in_features} network inputs")
+        W = -(-B // 64)
+        xw = torch.empty(F * nthr, W, dtype=torch.int64, device=self.device)
+        L.call("clb_pack_thresholds", L.dtype_code(x.dtype), L.ptr(x), B, F, x.stride(0), nthr, L.ptr(xw), W,
+               L.stream(self.device))
+        return xw
+
+    @torch.no_grad()
+    def forward_raw(self, x: torch.Tensor, nthr: int) -> torch.Tensor:
+        """Class counts of raw inputs binarised with nthr thresholds (input binarisation fused with packing)."""
+        L.require_cuda(x)
+        return self.counts_packed(self.pack_raw(x, nthr), x.shape[0])
+
     def _buffers(self, width: int):
         if self._bufs is None or self._bufs[0].shape[1] < width:
             rows = max(l.n_out for l in self.layers[:-1]) if len(self.layers) > 1 else 1
@@ -172,3 +195,36 @@ class PackedLogicNet:
 
     def predict(self, x: torch.Tensor) -> torch.Tensor:
         return self.forward(x).argmax(-1)
+
+
+def _state_prefixes(state):
+    return sorted({k.split(".")[0] for k in state if k.endswith(".weights") and k.split(".")[0].isdigit()}, key=int)
+
+
+def packed_from_state_dict(state: dict, input_dim: int, k: int, tau: float = 1.0, device="cuda",
+                           chunk_words: int = 128) -> PackedLogicNet:
+    """PackedLogicNet straight from a checkpoint's ``model_state`` of dense logic layers (the layout the
+    reference writes, experiments/experiment_script.py:520-541, and its compiler reads,
+    compiler/extract.py:49-98): per layer ``{i}.weights`` (out, K), ``{i}.indices`` (2, out, K),
+    ``{i}.gate_sequence`` (out, K); the gate of neuron j is the one at argmax_k weights[j, k] (first
+    maximum), as the compiler and the eval path choose it.  ``input_dim`` is the network's input width
+    (not recoverable from the state), ``k`` / ``tau`` the GroupSum parameters."""
+    layers = []
+    in_dim = int(input_dim)
+    for p in _state_prefixes(state):
+        w, idx, g = state[f"{p}.weights"], state[f"{p}.indices"], state[f"{p}.gate_sequence"]
+        out, K = w.shape
+        if tuple(idx.shape) != (2, out, K) or tuple(g.shape) != (out, K):
+            raise ValueError(f"layer {p}: unexpected buffer shapes")
+        layer = LogicLayer.__new__(LogicLayer)  # buffers only, no RNG-consuming constructor
+        torch.nn.Module.__init__(layer)
+        layer.in_dim, layer.out_dim, layer.num_gates = in_dim, out, K
+        layer.weights = torch.nn.Parameter(torch.as_tensor(w).float().to(device), requires_grad=False)
+        layer.register_buffer("indices", torch.as_tensor(idx).long().to(device))
+        layer.register_buffer("gate_sequence", torch.as_tensor(g).to(torch.uint8).to(device))
+        layer.is_frozen, layer._spec_key, layer._spec, layer._fused_groupsum = False, None, None, None
+        layers.append(layer)
+        in_dim = out
+    if not layers:
+        raise ValueError("no dense logic layers in the state dict")
+    return PackedLogicNet(torch.nn.Sequential(*layers, GroupSum(k, tau)), device=device, chunk_words=chunk_words)

@@ -224,6 +224,12 @@ int clb_cast(int src_dtype, const void* src, int dst_dtype, void* dst, int64_t n
 int clb_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, uint64_t* out,
                     int64_t ldw, clb_stream_t stream);
 
+/* Raw inputs x [batch, features] (e.g. pixels in [0,1]) -> nthr*features packed features: feature
+ * t*features + f is x[:, f] > (t+1)/(nthr+1), the reference's threshold binarisation
+ * (experiments/experiment_script.py:92, threshold-major channel order), fused with the packing. */
+int clb_pack_thresholds(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, int nthr,
+                        uint64_t* out, int64_t ldw, clb_stream_t stream);
+
 /* Frozen layer tables: sel_ab int32 [n_out, 2], sel_gate uint8 [n_out] from the slot table and the
  * per-row chosen slot (the `w` buffer of a frozen layer, or argmax of the logits; compactlogic.py:120-130). */
 int clb_packed_select(const int32_t* slots, const uint8_t* gates, const uint8_t* select, int64_t n_out, int64_t K,

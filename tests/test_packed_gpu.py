@@ -83,3 +83,27 @@ def test_packed_conv_net_matches_float_eval():
     x = (torch.rand(300, 3, 8, 8, device="cuda") < 0.5).float()
     counts = cl.PackedLogicNet(model, chunk_words=2)(x)
     np.testing.assert_array_equal(counts.cpu().numpy(), torch.round(model(x) * 2.0).to(torch.int32).cpu().numpy())
+
+
+def test_packed_from_checkpoint_state(golden):
+    """Checkpoint model_state -> packed network: class counts equal the reference circuit evaluator's."""
+    d = golden("discrete.npz")
+    state = {f"{i}.{n}": torch.from_numpy(d[f"{i}.{n}"]) for i in range(1, 4) for n in ("weights", "indices",
+                                                                                           "gate_sequence")}
+    net = cl.packed_from_state_dict(state, input_dim=784, k=int(d["k"]), tau=float(d["tau"]))
+    np.testing.assert_array_equal(net(cuda(d["x"].astype(np.float32))).cpu().numpy(), d["counts"])
+
+
+@pytest.mark.parametrize("B", [1, 100, 333])
+def test_fused_threshold_packing(B):
+    """Raw pixels -> thresholds -> packed bits in one kernel equals the reference binarisation
+    (experiments/experiment_script.py:92) followed by packing, and the network counts agree."""
+    torch.manual_seed(B)
+    model = torch.nn.Sequential(cl.ConvLayer((9, 8, 8), 1, 16, 3, 2, num_gates=8), torch.nn.Flatten(),
+                                cl.LogicLayer(256, 150, num_gates=8), cl.GroupSum(5, 1.0)).cuda().eval()
+    net = cl.PackedLogicNet(model)
+    px = torch.rand(B, 3, 8, 8)
+    binar = torch.cat([(px > (i + 1) / 4).float() for i in range(3)], dim=1)
+    np.testing.assert_array_equal(net.pack_raw(px.cuda(), 3).cpu().numpy().view(np.uint64),
+                                  O.pack_samples(binar.reshape(B, -1).numpy()))
+    np.testing.assert_array_equal(net.forward_raw(px.cuda(), 3).cpu().numpy(), net(binar.cuda()).cpu().numpy())
