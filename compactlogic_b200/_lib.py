@@ -47,9 +47,9 @@ _SIGS = {
                                   _p, _p, _sz, _p]),
     "clb_slots_dense": (_int, [_p, _p, _i64, _i64, _i64, _p, _p, _p]),
     "clb_slots_conv": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p, _p, _p]),
-    "clb_logic_forward": (_int, [_int, _p, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _p, _int, _p, _i64, _p,
+    "clb_logic_forward": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _p, _int, _p, _i64, _p,
                                  _i64, _i64, _i64, _p]),
-    "clb_logic_backward_chunks": (_i64, [_int, _p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64]),
+    "clb_logic_backward_chunks": (_i64, [_int, _p, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64]),
     "clb_logic_backward": (_int, [_int, _p, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _int, _p, _i64, _p, _i64,
                                   _i64, _i64, _dbl, _p, _i64, _int, _i64, _p, _i64, _p]),
     "clb_logic_grad_finalize": (_int, [_int, _p, _i64, _i64, _i64, _i64, _int, _p, _p, _p]),

@@ -56,8 +56,9 @@ struct Carve {
 
 LayerArgs layer(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots, int64_t n_out, int64_t K,
                 int64_t group, int mode, const void* weights, const uint8_t* gates, const uint8_t* select,
-                bool has_pad) {
+                bool has_pad, int64_t in_features = 0) {
     LayerArgs a{};
+    a.in_features = in_features;
     a.dtype = dtype;
     a.x = x;
     a.ldx = ldx;
@@ -121,7 +122,8 @@ int clb_slots_conv(const int32_t* och, const int8_t* oh, const int8_t* ow, int64
                        "slots_conv");
 }
 
-int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots, int64_t n_out,
+int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features, const int32_t* slots,
+                      int64_t n_out,
                       int64_t K, int64_t group, int weight_mode, const void* weights, const uint8_t* gates,
                       const uint8_t* select, int has_pad, void* y, int64_t ldy, void* gs_acc, int64_t gs_k,
                       int64_t gs_size, int64_t ld_gs, clb_stream_t stream) {
@@ -141,14 +143,16 @@ int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, cons
     } else {
         if (!y || ldy < ncols) return fail(CLB_ERR_INVALID, "forward: null y or ldy < ncols");
     }
-    const LayerArgs a = layer(dtype, x, ldx, ncols, slots, n_out, K, group, weight_mode, weights, gates, select, has_pad);
+    const LayerArgs a = layer(dtype, x, ldx, ncols, slots, n_out, K, group, weight_mode, weights, gates, select, has_pad,
+                              in_features);
     return cuda_status(launch_logic_forward(a, y, ldy, gs_acc ? &gs : nullptr, S(stream)), "logic_forward");
 }
 
-int64_t clb_logic_backward_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, const void* grad_y,
-                                  int64_t ldgy, const void* gs_grad, int64_t ld_gs, const void* grad_x, int64_t ldgx) {
+int64_t clb_logic_backward_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
+                                  const void* grad_y, int64_t ldgy, const void* gs_grad, int64_t ld_gs, const void* grad_x,
+                                  int64_t ldgx) {
     return logic_backward_chunks(dtype, ncols, ldx, x, grad_y ? ldgy : ncols, grad_y, gs_grad ? ld_gs : ncols, gs_grad,
-                                 grad_x ? ldgx : ncols, grad_x);
+                                 grad_x ? ldgx : ncols, grad_x, in_features);
 }
 
 int clb_logic_backward(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots, int64_t n_out,
@@ -182,9 +186,10 @@ int clb_logic_backward(int dtype, const void* x, int64_t ldx, int64_t ncols, con
         return fail(CLB_ERR_INVALID, "backward: null grad_y or ldgy < ncols");
     }
     const LayerArgs a = layer(dtype, x, ldx, ncols, slots, n_out, K, group, weight_mode, weights, gates, nullptr,
-                              has_pad);
+                              has_pad, in_features);
     if (partials) {
-        const int64_t need = clb_logic_backward_chunks(dtype, x, ldx, ncols, gs_grad ? nullptr : grad_y, ldgy, gs_grad,
+        const int64_t need = clb_logic_backward_chunks(dtype, x, ldx, ncols, in_features, gs_grad ? nullptr : grad_y, ldgy,
+                                                       gs_grad,
                                                        ld_gs, grad_x, ldgx);
         if (need != partials_chunks)
             return fail(CLB_ERR_INVALID, "backward: partials sized for %lld chunks, this call needs %lld",
@@ -313,7 +318,7 @@ int clb_difflogic_forward(int dtype, const void* x, int64_t in_dim, int64_t batc
     int32_t* slots = nullptr;
     int st = dense_common(dtype, x, in_dim, batch, a, b, out_dim, K, workspace, workspace_bytes, cv, slots, S(stream));
     if (st) return st;
-    return clb_logic_forward(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_PROBS, w, gate_seq, nullptr, 0, y,
+    return clb_logic_forward(dtype, x, batch, batch, in_dim, slots, out_dim, K, 1, CLB_W_PROBS, w, gate_seq, nullptr, 0, y,
                              batch, nullptr, 0, 0, 0, stream);
 }
 
@@ -324,7 +329,7 @@ int clb_difflogic_eval(int dtype, const void* x, int64_t in_dim, int64_t batch, 
     int32_t* slots = nullptr;
     int st = dense_common(dtype, x, in_dim, batch, a, b, out_dim, K, workspace, workspace_bytes, cv, slots, S(stream));
     if (st) return st;
-    return clb_logic_forward(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_SELECT, nullptr, gate_seq, w_sel, 0, y,
+    return clb_logic_forward(dtype, x, batch, batch, in_dim, slots, out_dim, K, 1, CLB_W_SELECT, nullptr, gate_seq, w_sel, 0, y,
                              batch, nullptr, 0, 0, 0, stream);
 }
 
@@ -335,7 +340,7 @@ int clb_difflogic_backward_w(int dtype, const void* x, int64_t in_dim, int64_t b
     int32_t* slots = nullptr;
     int st = dense_common(dtype, x, in_dim, batch, a, b, out_dim, K, workspace, workspace_bytes, cv, slots, S(stream));
     if (st) return st;
-    const int64_t chunks = clb_logic_backward_chunks(dtype, x, batch, batch, grad_y, batch, nullptr, 0, nullptr, 0);
+    const int64_t chunks = clb_logic_backward_chunks(dtype, x, batch, batch, in_dim, grad_y, batch, nullptr, 0, nullptr, 0);
     void* part = cv.take((size_t)std::max<int64_t>(chunks, 1) * out_dim * K * acc_size(dtype));
     if (!part) return fail(CLB_ERR_WORKSPACE, "workspace too small for partials");
     // d loss / d prob does not depend on the probabilities: no weights needed
@@ -464,7 +469,8 @@ static int conv_forward_impl(int dtype, const void* x, int64_t n, int64_t c_in, 
     if (st) return st;
     const int64_t hw = h_out * w_out, fout = c_out * hw;
     if (n == 0 || fout == 0) return CLB_OK;
-    st = clb_logic_forward(dtype, cw.xT, n, n, cw.slots, fout, K, hw, mode, w, gate_seq, sel, 1, cw.yT, n, nullptr, 0, 0,
+    st = clb_logic_forward(dtype, cw.xT, n, n, c_in * h_in * w_in, cw.slots, fout, K, hw, mode, w, gate_seq, sel, 1, cw.yT, n,
+                           nullptr, 0, 0,
                            0, stream);
     if (st) return st;
     return cuda_status(launch_transpose((int)esize(dtype), cw.yT, fout, n, n, y, fout, S(stream)), "transpose y");
@@ -524,9 +530,10 @@ int clb_convlogic_backward_w(int dtype, const void* x, int64_t n, int64_t c_in, 
         st = cuda_status(launch_transpose((int)e, grad_y, n, fout, fout, cw.gyT, n, S(stream)), "transpose grad_y");
         if (st) return st;
     }
-    const int64_t chunks = n > 0 ? clb_logic_backward_chunks(dtype, cw.xT, n, n, cw.gyT, n, nullptr, 0, nullptr, 0) : 0;
+    const int64_t chunks =
+        n > 0 ? clb_logic_backward_chunks(dtype, cw.xT, n, n, c_in * h_in * w_in, cw.gyT, n, nullptr, 0, nullptr, 0) : 0;
     st = clb_logic_backward(dtype, cw.xT, n, n, cw.slots, fout, K, hw, CLB_W_PROBS, nullptr, gate_seq, 1, cw.gyT, n,
-                            nullptr, 0, 0, 0, 0.0, nullptr, 0, 0, 0, cw.part, chunks, stream);
+                            nullptr, 0, 0, 0, 0.0, nullptr, 0, 0, c_in * h_in * w_in, cw.part, chunks, stream);
     if (st) return st;
     return clb_logic_grad_finalize(dtype, cw.part, chunks, fout, K, hw, CLB_W_PROBS, nullptr, grad_w, stream);
 }

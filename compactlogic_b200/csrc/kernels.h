@@ -26,6 +26,7 @@ struct LayerArgs {
     const uint8_t* gates;
     const uint8_t* select; // CLB_W_SELECT only: chosen slot per row
     bool has_pad;          // slots may contain -1
+    int64_t in_features;   // rows of x (0 = unknown); selects the column-chunk geometry
 };
 
 struct GroupSumArgs {
@@ -47,7 +48,8 @@ cudaError_t launch_logic_forward(const LayerArgs& a, void* y, int64_t ldy, const
 cudaError_t launch_logic_backward(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs* gs,
                                   void* gx, int64_t ldgx, void* partials, int64_t part_chunks, cudaStream_t s);
 int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void* x, int64_t ldgy,
-                              const void* gy, int64_t ld_gs, const void* gs_grad, int64_t ldgx, const void* gx);
+                              const void* gy, int64_t ld_gs, const void* gs_grad, int64_t ldgx, const void* gx,
+                              int64_t in_features);
 
 // partials [nchunks, n_out, K] -> per-row gradient [n_out / group, K]: w.r.t. the logits (softmax
 // backward fused) for CLB_W_LOGITS, w.r.t. the probabilities for CLB_W_PROBS.  `out_dtype` is the

@@ -387,6 +387,164 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
 }
 
 // ---------------------------------------------------------------------------------------------
+// Narrow-chunk variants for very wide inputs.  With 32*VEC columns per chunk, the slab of x (and of
+// grad_x) that one column chunk touches is in_features * 32*VEC elements — 1.5 GB for a 1M-wide layer —
+// so the gathers and scatter reductions of a chunk miss L2.  Here LPN lanes share a neuron (32/LPN
+// neurons per warp step) and a chunk is LPN*VEC columns, chosen on the host so the slab fits L2.
+// Each gather is still a whole 32-byte sector per lane group; the stage is read per lane group.
+// ---------------------------------------------------------------------------------------------
+template <typename T, int VEC, int LPN>
+__global__ void __launch_bounds__(kThreads)
+logic_forward_narrow_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, const GroupSumArgs gs,
+                            const bool use_gs, const int TN) {
+    using A = typename Acc<T>::type;
+    constexpr int G = 32 / LPN;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int K = a.K;
+    Stage<A> st = carve<A>(smem, TN, K, false);
+    const int64_t j0 = (int64_t)blockIdx.x * TN;
+    fill_stage<A, false>(a, j0, TN, st);
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lc = lane % LPN, sub = lane / LPN;
+    const int64_t col = (int64_t)blockIdx.y * (LPN * VEC) + lc * VEC;
+    const bool active = col < a.ncols;
+    const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
+    A gacc[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) gacc[i] = 0;
+    int64_t gcls = -1;
+    for (int t0 = warp * G; t0 < TN; t0 += kWarps * G) {
+        const int t = t0 + sub;
+        const int64_t j = j0 + t;
+        if (t >= TN || j >= a.n_out) continue;
+        A acc[VEC];
+        const A c0 = st.c0[t];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) acc[i] = c0;
+        if (active) {
+            const int ns = st.ns[t];
+            const int2* ab = st.ab + t * K;
+            const A4<A>* cf = st.cf + t * K;
+#pragma unroll 4
+            for (int s = 0; s < ns; ++s) {
+                const int2 pr = ab[s];
+                const A4<A> c = cf[s];
+                A va[VEC], vb[VEC];
+                gather<T, VEC>(x, pr.x, a.ldx, col, va);
+                gather<T, VEC>(x, pr.y, a.ldx, col, vb);
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) {
+                    const A u = fma(c.z, va[i], c.y);
+                    acc[i] = fma(c.x, va[i], acc[i]);
+                    acc[i] = fma(u, vb[i], acc[i]);
+                }
+            }
+        }
+        if (!use_gs) {
+            if (active) store_from_acc<T, VEC>(y + j * ldy + col, acc);
+        } else {
+            const int64_t cls = j / gs.size;
+            if (cls != gcls) {
+                if (gcls >= 0 && active) red_add<VEC>(reinterpret_cast<A*>(gs.acc) + gcls * gs.ld + col, gacc);
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) gacc[i] = 0;
+                gcls = cls;
+            }
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) gacc[i] += acc[i];
+        }
+    }
+    if (use_gs && gcls >= 0 && active) red_add<VEC>(reinterpret_cast<A*>(gs.acc) + gcls * gs.ld + col, gacc);
+}
+
+template <typename T, int VEC, int LPN, int KT>
+__global__ void __launch_bounds__(kThreads)
+logic_backward_narrow_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict__ gy, const int64_t ldgy,
+                             const GroupSumArgs gs, const bool use_gs, typename Acc<T>::type* __restrict__ gx,
+                             const int64_t ldgx, typename Acc<T>::type* __restrict__ part, const int TN) {
+    using A = typename Acc<T>::type;
+    constexpr int G = 32 / LPN;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int K = KT > 0 ? KT : a.K;
+    Stage<A> st = carve<A>(smem, TN, K, true);
+    const int64_t j0 = (int64_t)blockIdx.x * TN;
+    fill_stage<A, true>(a, j0, TN, st);
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lc = lane % LPN, sub = lane / LPN;
+    const int64_t chunk = blockIdx.y;
+    const int64_t col = chunk * (LPN * VEC) + lc * VEC;
+    const bool active = col < a.ncols;
+    const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
+    const A* gsg = reinterpret_cast<const A*>(gs.grad);
+    for (int t0 = warp * G; t0 < TN; t0 += kWarps * G) {  // warp-uniform trip count (segment shuffles)
+        const int t = t0 + sub;
+        const int64_t j = j0 + t;
+        const bool valid = t < TN && j < a.n_out;
+        const bool live = valid && active;
+        const int ts = valid ? t : 0;
+        A g[VEC];
+        if (live) {
+            if (use_gs) {
+                load_acc<A, VEC>(gsg + (j / gs.size) * gs.ld + col, g);
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) g[i] *= (A)gs.scale;
+            } else {
+                load_acc<A, VEC>(gy + j * ldgy + col, g);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) g[i] = 0;
+        }
+        const int2* ab = st.ab + ts * K;
+        const A4<A>* cf = st.cf + ts * K;
+        const A* pp = st.p + ts * K;
+        A pk[KT > 0 ? KT : 1];
+#pragma unroll(KT > 0 ? KT : 4)
+        for (int s = 0; s < K; ++s) {
+            const int2 pr = live ? ab[s] : make_int2(-1, -1);
+            const A4<A> c = cf[s];
+            A va[VEC], vb[VEC];
+            gather<T, VEC>(x, pr.x, a.ldx, col, va);
+            gather<T, VEC>(x, pr.y, a.ldx, col, vb);
+            A dot = 0;
+            A da[VEC], db[VEC];
+            const A pw = pp[s];
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                const A dfdb = fma(c.w, va[i], c.z);
+                const A dfda = fma(c.w, vb[i], c.y);
+                const A f = fma(dfdb, vb[i], fma(c.y, va[i], c.x));
+                dot = fma(g[i], f, dot);
+                const A pg = pw * g[i];
+                da[i] = dfda * pg;
+                db[i] = dfdb * pg;
+            }
+            if (gx != nullptr) {
+                if (pr.x >= 0) red_add<VEC>(gx + (int64_t)pr.x * ldgx + col, da);
+                if (pr.y >= 0) red_add<VEC>(gx + (int64_t)pr.y * ldgx + col, db);
+            }
+            if (KT > 0) {
+                pk[KT > 0 ? s : 0] = dot;
+            } else if (part != nullptr) {
+                dot = seg_sum(dot, LPN);
+                if (lc == 0 && valid) part[(chunk * a.n_out + j) * K + s] = dot;
+            }
+        }
+        if (KT > 0 && part != nullptr) {
+#pragma unroll
+            for (int s = 0; s < (KT > 0 ? KT : 1); ++s) {
+                const A v = seg_sum(pk[s], LPN);
+                if (lc == 0 && valid) part[(chunk * a.n_out + j) * K + s] = v;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Finalize: sum partials over chunks (and over the group of neurons sharing a parameter row), then
 // for logits apply the softmax backward  dL/dw_k = p_k (g_k - sum_i p_i g_i)  (torch softmax
 // backward, compactlogic.py:108 + autograd).
@@ -606,6 +764,17 @@ int bwd_minb() {
     return v == 5 ? 5 : 1;
 }
 
+// Column-chunk width: the slab (in_features x chunk columns x bytes per element) of one chunk should
+// stay in L2; very wide inputs get LPN < 32 lanes per neuron (narrow chunks).
+constexpr size_t kSlabBudget = size_t(96) << 20;
+int pick_lpn(int64_t in_features, int V, size_t bytes) {
+    if (in_features <= 0) return 32;
+    if ((size_t)in_features * 32 * V * bytes <= kSlabBudget) return 32;
+    for (int l = 16; l >= 2; l >>= 1)
+        if ((size_t)in_features * l * V * bytes <= kSlabBudget) return l;
+    return 2;
+}
+
 int choose_tn(size_t bytes_per_neuron) {
     int tn = tn_max();
     while (tn > 8 && bytes_per_neuron * tn > 96 * 1024) tn >>= 1;
@@ -643,6 +812,77 @@ bool can_vec(int64_t ncols, std::initializer_list<int64_t> lds, std::initializer
     return true;
 }
 
+template <typename T, int LPN>
+cudaError_t fwd_narrow_l(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s) {
+    using A = typename Acc<T>::type;
+    constexpr int V = vmax<T>();
+    const int TN = kWarps * (32 / LPN);
+    const size_t smem = stage_bytes<A>(TN, a.K, false);
+    GroupSumArgs g{};
+    if (gs) g = *gs;
+    dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, LPN * V));
+    if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+    auto k = logic_forward_narrow_kernel<T, V, LPN>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t fwd_narrow(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, int lpn, cudaStream_t s) {
+    switch (lpn) {
+        case 16: return fwd_narrow_l<T, 16>(a, y, ldy, gs, s);
+        case 8: return fwd_narrow_l<T, 8>(a, y, ldy, gs, s);
+        case 4: return fwd_narrow_l<T, 4>(a, y, ldy, gs, s);
+        default: return fwd_narrow_l<T, 2>(a, y, ldy, gs, s);
+    }
+}
+
+template <typename T, int LPN, int KT>
+cudaError_t bwd_narrow_k(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs& g, bool use_gs, void* gx,
+                         int64_t ldgx, void* part, cudaStream_t s) {
+    using A = typename Acc<T>::type;
+    constexpr int V = vmax<T>();
+    const int TN = kWarps * (32 / LPN);
+    const size_t smem = stage_bytes<A>(TN, a.K, true);
+    dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, LPN * V));
+    if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+    auto k = logic_backward_narrow_kernel<T, V, LPN, KT>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<const A*>(gy), ldgy, g, use_gs, reinterpret_cast<A*>(gx), ldgx,
+                                   reinterpret_cast<A*>(part), TN);
+    return cudaGetLastError();
+}
+
+template <typename T, int LPN>
+cudaError_t bwd_narrow_l(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs& g, bool use_gs, void* gx,
+                         int64_t ldgx, void* part, cudaStream_t s) {
+    switch (a.K) {
+        case 4: return bwd_narrow_k<T, LPN, 4>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+        case 8: return bwd_narrow_k<T, LPN, 8>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+        case 16: return bwd_narrow_k<T, LPN, 16>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+        default: return bwd_narrow_k<T, LPN, 0>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+    }
+}
+
+template <typename T>
+cudaError_t bwd_narrow(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs& g, bool use_gs, void* gx,
+                       int64_t ldgx, void* part, int lpn, cudaStream_t s) {
+    switch (lpn) {
+        case 16: return bwd_narrow_l<T, 16>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+        case 8: return bwd_narrow_l<T, 8>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+        case 4: return bwd_narrow_l<T, 4>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+        default: return bwd_narrow_l<T, 2>(a, gy, ldgy, g, use_gs, gx, ldgx, part, s);
+    }
+}
+
+template <typename T>
+int bwd_lpn(const LayerArgs& a, bool vec, int V, const void* gx) {
+    using A = typename Acc<T>::type;
+    if (!vec || V != vmax<T>() || std::is_same<T, double>::value) return 32;
+    return pick_lpn(a.in_features, V, sizeof(T) + (gx != nullptr ? sizeof(A) : 0));
+}
+
 template <typename T>
 cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s) {
     using A = typename Acc<T>::type;
@@ -659,6 +899,9 @@ cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* 
     const int V = vec ? (half ? 2 : wide ? 8 : vmax<T>()) : 1;
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+    const int lpn = (vec && !wide && !half && !std::is_same<T, double>::value) ? pick_lpn(a.in_features, V, sizeof(T))
+                                                                                  : 32;
+    if (lpn < 32) return fwd_narrow<T>(a, y, ldy, gs, lpn, s);
     if (wide) {
         auto k = logic_forward_kernel<T, 8>;
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -735,6 +978,11 @@ cudaError_t bwd_t(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupS
     const bool wide = vec && bv == 8 && bwd_wide_ok(a, ldgy, gs, ldgx);
     const bool half = vec && bv == 2;
     const int V = vec ? (half ? 2 : wide ? 8 : vmax<T>()) : 1;
+    const int lpn = bwd_lpn<T>(a, vec, V, gx);
+    if (lpn < 32) {
+        if (part != nullptr && ceil_div64(a.ncols, lpn * V) != part_chunks) return cudaErrorInvalidValue;
+        return bwd_narrow<T>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, lpn, s);
+    }
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (part != nullptr && (int64_t)grid.y != part_chunks) return cudaErrorInvalidValue;  // scratch sized for another split
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
@@ -783,7 +1031,7 @@ cudaError_t launch_logic_backward(const LayerArgs& a, const void* gy, int64_t ld
 }
 
 int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void* x, int64_t ldgy, const void* gy,
-                              int64_t ld_gs, const void* gs_grad, int64_t ldgx, const void* gx) {
+                              int64_t ld_gs, const void* gs_grad, int64_t ldgx, const void* gx, int64_t in_features) {
     GroupSumArgs g{};
     g.grad = gs_grad;
     g.ld = ld_gs;
@@ -794,19 +1042,30 @@ int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void*
     a.ncols = ncols;
     a.ldx = ldx;
     a.x = x;
+    a.in_features = in_features;
     bool vec = false;
-    int vm = 1;
+    int v = 1, lpn = 32;
     switch (dtype) {
-        case CLB_F32:
+        case CLB_F32: {
             vec = bwd_vec<float>(a, gy, ldgy, gs, gx, ldgx);
-            vm = bwd_vec_f32();
-            if (vm == 8 && !bwd_wide_ok(a, gs ? 0 : ldgy, gs, ldgx)) vm = 4;
+            const int bv = bwd_vec_f32();
+            const bool wide = vec && bv == 8 && bwd_wide_ok(a, gs ? 0 : ldgy, gs, ldgx);
+            v = vec ? (bv == 2 ? 2 : wide ? 8 : 4) : 1;
+            lpn = bwd_lpn<float>(a, vec, v, gx);
             break;
-        case CLB_F64: vec = bwd_vec<double>(a, gy, ldgy, gs, gx, ldgx); vm = vmax<double>(); break;
-        case CLB_BF16: vec = bwd_vec<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx); vm = vmax<__nv_bfloat16>(); break;
+        }
+        case CLB_F64:
+            vec = bwd_vec<double>(a, gy, ldgy, gs, gx, ldgx);
+            v = vec ? vmax<double>() : 1;
+            break;
+        case CLB_BF16:
+            vec = bwd_vec<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx);
+            v = vec ? vmax<__nv_bfloat16>() : 1;
+            lpn = bwd_lpn<__nv_bfloat16>(a, vec, v, gx);
+            break;
         default: return -1;
     }
-    return ceil_div64(ncols, 32 * (vec ? vm : 1));
+    return ceil_div64(ncols, lpn * v);
 }
 
 cudaError_t launch_grad_finalize(const LayerArgs& a, const void* partials, int64_t nchunks, void* out, int out_dtype,

@@ -66,7 +66,8 @@ extern "C" int clb_difflogic_backward_w_noalloc(int dtype, const void* x, int64_
         return clb::set_error(CLB_ERR_INVALID, "null pointer");
     const size_t acc = dtype == CLB_F64 ? 8 : 4;
     const int64_t chunks =
-        batch > 0 ? clb::logic_backward_chunks(dtype, batch, batch, x, batch, grad_y, 0, nullptr, batch, nullptr) : 0;
+        batch > 0 ? clb::logic_backward_chunks(dtype, batch, batch, x, batch, grad_y, 0, nullptr, batch, nullptr, in_dim)
+                  : 0;
     const size_t slot_bytes = round256((size_t)out_dim * K * 8);
     const size_t need = slot_bytes + round256((size_t)chunks * out_dim * K * acc);
     if (need > kNoAllocScratchBytes)
@@ -93,6 +94,7 @@ extern "C" int clb_difflogic_backward_w_noalloc(int dtype, const void* x, int64_
     la.group = 1;
     la.mode = CLB_W_PROBS;
     la.gates = gate_seq;
+    la.in_features = in_dim;
     if (batch > 0) {
         e = clb::launch_logic_backward(la, grad_y, batch, nullptr, nullptr, 0, part, chunks, s);
         if (e != cudaSuccess) return clb::set_error(CLB_ERR_CUDA, cudaGetErrorString(e));

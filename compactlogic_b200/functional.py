@@ -84,7 +84,8 @@ def forward_into(xt: torch.Tensor, weights: Optional[torch.Tensor], spec: LayerS
     e = xt.element_size()
     nbytes = e * B * (spec.in_features + (spec.n_out if y is not None else 0)) + _param_bytes(spec)
     TIMER.launch("forward" if mode != L.W_SELECT else "eval", nbytes, lambda: L.call(
-        "clb_logic_forward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
+        "clb_logic_forward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, spec.in_features, L.ptr(spec.slots),
+        spec.n_out,
         spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), L.ptr(select), int(spec.has_pad), L.ptr(y),
         y.stride(0) if y is not None else 0, L.ptr(gs_acc), gs_acc.shape[0] if gs_acc is not None else 0, gs_size,
         gs_acc.stride(0) if gs_acc is not None else 0, L.stream(xt.device)))
@@ -103,7 +104,8 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
     part = None
     chunks = 0
     if need_gw:
-        chunks = int(L.lib().clb_logic_backward_chunks(L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, gy_ptr,
+        chunks = int(L.lib().clb_logic_backward_chunks(L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B,
+                                                       spec.in_features, gy_ptr,
                                                        ldgy, gs_ptr, ld_gs, L.ptr(gx), B))
         part = torch.empty(max(chunks, 1), spec.n_out, spec.K, dtype=acc, device=dev)
     a = torch.empty((), dtype=acc).element_size()

@@ -181,19 +181,23 @@ int clb_slots_conv(const int32_t* offsets_ch, const int8_t* offsets_h, const int
                    int64_t K, int64_t c_in, int64_t h_in, int64_t w_in, int64_t h_out, int64_t w_out, int stride,
                    int32_t* slots, int32_t* err, clb_stream_t stream);
 
+/* in_features = rows of x: with the column count it selects the column-chunk geometry (very wide inputs
+ * use narrower chunks so a chunk's slab of x stays in L2). */
 /* Forward of one layer over columns [0, ncols) (LogicLayer.forward_cuda + LogicLayerCudaFunction.forward,
  * compactlogic.py:83-118,483-486; eval with mode CLB_W_SELECT, compactlogic.py:120-130).
  * If gs_acc != NULL the layer's GroupSum (compactlogic.py:450-468) is fused: y is not written and
  * gs_acc [gs_k, ld_gs] (arithmetic type, pre-zeroed) accumulates sum over the neurons of each class,
  * class(j) = j / gs_size. */
-int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots, int64_t n_out,
+int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features, const int32_t* slots,
+                      int64_t n_out,
                       int64_t K, int64_t group, int weight_mode, const void* weights, const uint8_t* gates,
                       const uint8_t* select, int has_pad, void* y, int64_t ldy, void* gs_acc, int64_t gs_k,
                       int64_t gs_size, int64_t ld_gs, clb_stream_t stream);
 
 /* Number of column chunks of the backward pass = rows of the partials scratch [nchunks, n_out, K]. */
-int64_t clb_logic_backward_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, const void* grad_y,
-                                  int64_t ldgy, const void* gs_grad, int64_t ld_gs, const void* grad_x, int64_t ldgx);
+int64_t clb_logic_backward_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
+                                  const void* grad_y, int64_t ldgy, const void* gs_grad, int64_t ld_gs, const void* grad_x,
+                                  int64_t ldgx);
 
 /* Fused backward of one layer (LogicLayerCudaFunction.backward, compactlogic.py:488-508):
  *  - grad_x (optional, [in, ldgx] arithmetic type): activation gradient; zeroed first when zero_grad_x.

@@ -31,7 +31,7 @@ def test_errors_are_reported_not_fatal():
     L = _lib.lib()
     assert L.clb_abi_version() == 1
     # invalid arguments are rejected before any CUDA call (works without a GPU)
-    st = L.clb_logic_forward(7, None, 0, 0, None, 0, 1, 1, 0, None, None, None, 0, None, 0, None, 0, 0, 0, None)
+    st = L.clb_logic_forward(7, None, 0, 0, 0, None, 0, 1, 1, 0, None, None, None, 0, None, 0, None, 0, 0, 0, None)
     assert st == _lib.CLB_ERR_DTYPE
     assert b"dtype" in L.clb_last_error()
     st = L.clb_groupbitsum(None, 10, 1, 64, 0, 3, None, None)

@@ -191,3 +191,28 @@ def test_bf16_chain_keeps_fp32_gradients():
         gw = O.softmax_backward(p, O.dense_backward_w(h[li], idx[0], idx[1], g, gy))
         assert_close(layers[li].weights.grad, gw, 1e-2, f"bf16 grad layer {li}")
         gy = O.dense_backward_x(h[li], idx[0], idx[1], p, g, gy)
+
+
+@pytest.mark.parametrize("dtype,in_dim,out,K,B", [(torch.float32, 300000, 150000, 4, 256),
+                                                 (torch.bfloat16, 600000, 300000, 4, 128)])
+def test_narrow_chunks_for_very_wide_inputs(dtype, in_dim, out, K, B):
+    """Inputs so wide that a 32-lane column chunk's slab would not fit L2 switch to narrow chunks
+    (several neurons per warp); results are unchanged."""
+    x, a, b, logits, g, gy = rand_dense(11, in_dim, out, K, B)
+    spec = _spec(a, b, g, in_dim)
+    xt = cuda(x, dtype)
+    wide_chunks = B // (32 * (16 // xt.element_size()))
+    n = L.lib().clb_logic_backward_chunks(L.dtype_code(dtype), xt.data_ptr(), B, B, in_dim, 1, B, None, 0, 1, B)
+    assert n > wide_chunks  # the narrow geometry is in use
+    xt.requires_grad_(True)
+    w = cuda(logits, torch.float32).requires_grad_(True)
+    y = LogicLayerFn.apply(xt, w, spec)
+    xr = xt.detach().double().cpu().numpy()
+    p = O.softmax(logits)
+    tol = RTOL[dtype]
+    assert_close(y, O.dense_forward(xr, a, b, p, g), tol, "narrow y")
+    y.backward(cuda(gy, dtype))
+    gyr = cuda(gy, dtype).double().cpu().numpy()
+    assert_close(w.grad, O.softmax_backward(p, O.dense_backward_w(xr, a, b, g, gyr)), tol, "narrow grad_logits")
+    if dtype == torch.float32:
+        assert_close(xt.grad, O.dense_backward_x(xr, a, b, p, g, gyr), tol, "narrow grad_x")
