@@ -767,7 +767,16 @@ int bwd_minb() {
 // Column-chunk width: the slab (in_features x chunk columns x bytes per element) of one chunk should
 // stay in L2; very wide inputs get LPN < 32 lanes per neuron (narrow chunks).
 constexpr size_t kSlabBudget = size_t(96) << 20;
-int pick_lpn(int64_t in_features, int V, size_t bytes) {
+// CLB_FWD_LPN / CLB_BWD_LPN force the lanes per neuron (tuning; 32 = always the full-warp chunk).
+int forced_lpn(bool backward) {
+    static const int f = env_int("CLB_FWD_LPN", 0);
+    static const int b = env_int("CLB_BWD_LPN", 0);
+    const int v = backward ? b : f;
+    return (v == 2 || v == 4 || v == 8 || v == 16 || v == 32) ? v : 0;
+}
+
+int pick_lpn(int64_t in_features, int V, size_t bytes, bool backward) {
+    if (forced_lpn(backward)) return forced_lpn(backward);
     if (in_features <= 0) return 32;
     if ((size_t)in_features * 32 * V * bytes <= kSlabBudget) return 32;
     for (int l = 16; l >= 2; l >>= 1)
@@ -880,7 +889,7 @@ template <typename T>
 int bwd_lpn(const LayerArgs& a, bool vec, int V, const void* gx) {
     using A = typename Acc<T>::type;
     if (!vec || V != vmax<T>() || std::is_same<T, double>::value) return 32;
-    return pick_lpn(a.in_features, V, sizeof(T) + (gx != nullptr ? sizeof(A) : 0));
+    return pick_lpn(a.in_features, V, sizeof(T) + (gx != nullptr ? sizeof(A) : 0), true);
 }
 
 template <typename T>
@@ -899,7 +908,7 @@ cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* 
     const int V = vec ? (half ? 2 : wide ? 8 : vmax<T>()) : 1;
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-    const int lpn = (vec && !wide && !half && !std::is_same<T, double>::value) ? pick_lpn(a.in_features, V, sizeof(T))
+    const int lpn = (vec && !wide && !half && !std::is_same<T, double>::value) ? pick_lpn(a.in_features, V, sizeof(T), false)
                                                                                   : 32;
     if (lpn < 32) return fwd_narrow<T>(a, y, ldy, gs, lpn, s);
     if (wide) {
