@@ -764,9 +764,7 @@ int bwd_minb() {
     return v == 5 ? 5 : 1;
 }
 
-// Column-chunk width: the slab (in_features x chunk columns x bytes per element) of one chunk should
-// stay in L2; very wide inputs get LPN < 32 lanes per neuron (narrow chunks).
-constexpr size_t kSlabBudget = size_t(96) << 20;
+// Column-chunk width: LPN lanes per neuron (32 = one neuron per warp step, 32*VEC columns per chunk).
 // CLB_FWD_LPN / CLB_BWD_LPN force the lanes per neuron (tuning; 32 = always the full-warp chunk).
 int forced_lpn(bool backward) {
     static const int f = env_int("CLB_FWD_LPN", 0);
@@ -776,12 +774,13 @@ int forced_lpn(bool backward) {
 }
 
 int pick_lpn(int64_t in_features, int V, size_t bytes, bool backward) {
-    if (forced_lpn(backward)) return forced_lpn(backward);
-    if (in_features <= 0) return 32;
-    if ((size_t)in_features * 32 * V * bytes <= kSlabBudget) return 32;
-    for (int l = 16; l >= 2; l >>= 1)
-        if ((size_t)in_features * l * V * bytes <= kSlabBudget) return l;
-    return 2;
+    // Measured on B200 (c5: 1M-wide inputs, bf16): narrow chunks keep the slab in L2 but cost 4-16x
+    // more LSU wavefronts per byte and were slower at every width tried, so the full-warp chunk is
+    // the default and the narrow kernels are opt-in.
+    (void)in_features;
+    (void)V;
+    (void)bytes;
+    return forced_lpn(backward) ? forced_lpn(backward) : 32;
 }
 
 int choose_tn(size_t bytes_per_neuron) {

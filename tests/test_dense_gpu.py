@@ -193,11 +193,8 @@ def test_bf16_chain_keeps_fp32_gradients():
         gy = O.dense_backward_x(h[li], idx[0], idx[1], p, g, gy)
 
 
-@pytest.mark.parametrize("dtype,in_dim,out,K,B", [(torch.float32, 300000, 150000, 4, 256),
-                                                 (torch.bfloat16, 600000, 300000, 4, 128)])
-def test_narrow_chunks_for_very_wide_inputs(dtype, in_dim, out, K, B):
-    """Inputs so wide that a 32-lane column chunk's slab would not fit L2 switch to narrow chunks
-    (several neurons per warp); results are unchanged."""
+def _narrow_case(dtype_name, in_dim, out, K, B):
+    dtype = getattr(torch, dtype_name)
     x, a, b, logits, g, gy = rand_dense(11, in_dim, out, K, B)
     spec = _spec(a, b, g, in_dim)
     xt = cuda(x, dtype)
@@ -216,3 +213,20 @@ def test_narrow_chunks_for_very_wide_inputs(dtype, in_dim, out, K, B):
     assert_close(w.grad, O.softmax_backward(p, O.dense_backward_w(xr, a, b, g, gyr)), tol, "narrow grad_logits")
     if dtype == torch.float32:
         assert_close(xt.grad, O.dense_backward_x(xr, a, b, p, g, gyr), tol, "narrow grad_x")
+
+
+@pytest.mark.parametrize("dtype,in_dim,out,K,B,lpn", [("float32", 30000, 20000, 4, 256, 2),
+                                                     ("float32", 30000, 20000, 16, 200, 8),
+                                                     ("bfloat16", 60000, 30000, 4, 128, 4)])
+def test_narrow_chunks_opt_in(dtype, in_dim, out, K, B, lpn):
+    """The opt-in narrow-chunk kernels (several neurons per warp; CLB_FWD_LPN / CLB_BWD_LPN, read once per
+    process, hence a child process) give the same results."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, CLB_FWD_LPN=str(lpn), CLB_BWD_LPN=str(lpn))
+    code = ("import sys; sys.path[:0] = ['tests', '.']; import test_dense_gpu as t; "
+            f"t._narrow_case({dtype!r}, {in_dim}, {out}, {K}, {B})")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
