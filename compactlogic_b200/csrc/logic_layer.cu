@@ -31,62 +31,35 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-// One candidate-gate slot as staged in shared memory: both operand ids (-1 = not read), the gate's
-// probability and the gate id — one 16-byte shared load per slot for fp32.  The gate's polynomial
-// coefficients come from kGatePoly through the constant cache (the id is warp-uniform in the
-// full-warp kernels), not from shared memory.
-template <typename A> struct alignas(16) SlotRec {
-    int a, b;
-    A p;
-    int g;
-};
-
-// c0..c3 of gate id i, derived from its truth-table bits (gates.cuh gate_poly).
-#define CLB_T00(i) (((i) >> 3) & 1)
-#define CLB_T01(i) (((i) >> 2) & 1)
-#define CLB_T10(i) (((i) >> 1) & 1)
-#define CLB_T11(i) ((i) & 1)
-#define CLB_GATE_POLY(i)                                                                              \
-    {(float)CLB_T00(i), (float)(CLB_T10(i) - CLB_T00(i)), (float)(CLB_T01(i) - CLB_T00(i)),          \
-     (float)(CLB_T00(i) - CLB_T01(i) - CLB_T10(i) + CLB_T11(i))}
-__constant__ float4 kGatePoly[16] = {CLB_GATE_POLY(0),  CLB_GATE_POLY(1),  CLB_GATE_POLY(2),  CLB_GATE_POLY(3),
-                                     CLB_GATE_POLY(4),  CLB_GATE_POLY(5),  CLB_GATE_POLY(6),  CLB_GATE_POLY(7),
-                                     CLB_GATE_POLY(8),  CLB_GATE_POLY(9),  CLB_GATE_POLY(10), CLB_GATE_POLY(11),
-                                     CLB_GATE_POLY(12), CLB_GATE_POLY(13), CLB_GATE_POLY(14), CLB_GATE_POLY(15)};
-
 template <typename A> struct A4 { A x, y, z, w; };
 
 // Shared-memory slot stage for TN neurons.
 template <typename A> struct Stage {
-    SlotRec<A>* rec;  // [TN*K]
-    A* c0;            // [TN]   forward: sum_k p*c0
-    int* ns;          // [TN]   number of active slots
+    A4<A>* cf;   // [TN*K] forward: p*c1, p*c2, p*c3 ; backward: c0, c1, c2, c3 (raw)
+    int2* ab;    // [TN*K]
+    A* p;        // [TN*K] backward only
+    A* c0;       // [TN]   forward: sum_k p*c0
+    int* ns;     // [TN]   number of active slots
 };
 
 template <typename A>
 __host__ __device__ inline size_t stage_bytes(int TN, int K, bool backward) {
-    (void)backward;
-    return (size_t)TN * K * sizeof(SlotRec<A>) + (size_t)TN * (sizeof(A) + sizeof(int));
+    size_t b = (size_t)TN * K * (sizeof(A4<A>) + sizeof(int2)) + (size_t)TN * (sizeof(A) + sizeof(int));
+    if (backward) b += (size_t)TN * K * sizeof(A);
+    return b;
 }
 
 template <typename A>
 __device__ __forceinline__ Stage<A> carve(unsigned char* smem, int TN, int K, bool backward) {
-    (void)backward;
     Stage<A> s;
-    s.rec = reinterpret_cast<SlotRec<A>*>(smem);
-    s.c0 = reinterpret_cast<A*>(s.rec + (size_t)TN * K);
+    s.cf = reinterpret_cast<A4<A>*>(smem);
+    s.ab = reinterpret_cast<int2*>(s.cf + (size_t)TN * K);
+    A* after = reinterpret_cast<A*>(s.ab + (size_t)TN * K);
+    s.p = after;
+    if (backward) after += (size_t)TN * K;
+    s.c0 = after;
     s.ns = reinterpret_cast<int*>(s.c0 + TN);
     return s;
-}
-
-template <typename A>
-__device__ __forceinline__ SlotRec<A> make_rec(int2 ab, A p, int g) {
-    SlotRec<A> r;
-    r.a = ab.x;
-    r.b = ab.y;
-    r.p = p;
-    r.g = g;
-    return r;
 }
 
 // Operands a gate does not depend on are marked -1, so neither the forward gather nor the backward
@@ -143,9 +116,14 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
             }
             GatePoly gp{0.f, 0.f, 0.f, 0.f};
             if (valid) {
-                const int gid = a.gates[r * K + k] & 15;
-                gp = gate_poly(gid);
-                st.rec[e] = make_rec<A>(used_operands(slots[j * K + k], gp), p, gid);
+                gp = gate_poly(a.gates[r * K + k] & 15);
+                st.ab[e] = used_operands(slots[j * K + k], gp);
+                if (BACKWARD) {
+                    st.cf[e] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
+                    st.p[e] = p;
+                } else {
+                    st.cf[e] = A4<A>{p * (A)gp.c1, p * (A)gp.c2, p * (A)gp.c3, (A)0};
+                }
             }
             const A c0sum = seg_sum(p * (A)gp.c0, K);
             if (e < total && k == 0) {
@@ -165,10 +143,15 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
             if (a.mode == CLB_W_SELECT) {
                 const int k = a.select[r];
                 if (k < K) {
-                    const int gid = g[k] & 15;
-                    const GatePoly gp = gate_poly(gid);
-                    st.rec[t * K] = make_rec<A>(used_operands(slots[j * K + k], gp), (A)1, gid);
-                    c0sum = (A)gp.c0;
+                    const GatePoly gp = gate_poly(g[k] & 15);
+                    st.ab[t * K] = used_operands(slots[j * K + k], gp);
+                    if (BACKWARD) {
+                        st.cf[t * K] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
+                        st.p[t * K] = (A)1;
+                    } else {
+                        st.cf[t * K] = A4<A>{(A)gp.c1, (A)gp.c2, (A)gp.c3, (A)0};
+                        c0sum = (A)gp.c0;
+                    }
                     ns = 1;
                 }
             } else {
@@ -182,10 +165,15 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
                 }
                 for (int k = 0; k < K; ++k) {
                     const A p = a.mode == CLB_W_LOGITS ? exp_acc(wr[k] - m) / sum : (w != nullptr ? wr[k] : (A)0);
-                    const int gid = g[k] & 15;
-                    const GatePoly gp = gate_poly(gid);
-                    st.rec[t * K + k] = make_rec<A>(used_operands(slots[j * K + k], gp), p, gid);
-                    c0sum += p * (A)gp.c0;
+                    const GatePoly gp = gate_poly(g[k] & 15);
+                    st.ab[t * K + k] = used_operands(slots[j * K + k], gp);
+                    if (BACKWARD) {
+                        st.cf[t * K + k] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
+                        st.p[t * K + k] = p;
+                    } else {
+                        st.cf[t * K + k] = A4<A>{p * (A)gp.c1, p * (A)gp.c2, p * (A)gp.c3, (A)0};
+                        c0sum += p * (A)gp.c0;
+                    }
                 }
                 ns = K;
             }
@@ -243,13 +231,12 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
         for (int i = 0; i < VEC; ++i) acc[i] = c0;
         if (active) {
             const int ns = st.ns[t];
-            const SlotRec<A>* rec = st.rec + t * K;
+            const int2* ab = st.ab + t * K;
+            const A4<A>* cf = st.cf + t * K;
 #pragma unroll UNR
             for (int s = 0; s < ns; ++s) {
-                const SlotRec<A> r = rec[s];
-                const int2 pr = make_int2(r.a, r.b);
-                const float4 cg = kGatePoly[r.g];
-                const A4<A> c{r.p * (A)cg.y, r.p * (A)cg.z, r.p * (A)cg.w, (A)0};  // p*c1, p*c2, p*c3
+                const int2 pr = ab[s];
+                const A4<A> c = cf[s];
                 A va[VEC], vb[VEC];
                 gather<T, VEC>(x, pr.x, a.ldx, col, va);
                 gather<T, VEC>(x, pr.y, a.ldx, col, vb);
@@ -349,15 +336,15 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
 #pragma unroll
             for (int i = 0; i < VEC; ++i) g[i] = 0;
         }
-        const SlotRec<A>* rec = st.rec + t * K;
+        const int2* ab = st.ab + t * K;
+        const A4<A>* cf = st.cf + t * K;
+        const A* pp = st.p + t * K;
         A pk[KT > 0 ? KT : 1];
 
 #pragma unroll(KT > 0 ? KT : 4)
         for (int s = 0; s < K; ++s) {
-            const SlotRec<A> r = rec[s];
-            const int2 pr = make_int2(r.a, r.b);
-            const float4 cg = kGatePoly[r.g];
-            const A4<A> c{(A)cg.x, (A)cg.y, (A)cg.z, (A)cg.w};  // raw c0..c3
+            const int2 pr = ab[s];
+            const A4<A> c = cf[s];
             A va[VEC], vb[VEC];
             if (active) {
                 gather<T, VEC>(x, pr.x, a.ldx, col, va);
@@ -368,7 +355,7 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
             }
             A dot = 0;
             A da[VEC], db[VEC];
-            const A pw = r.p;
+            const A pw = pp[s];
 #pragma unroll
             for (int i = 0; i < VEC; ++i) {
                 const A dfdb = fma(c.w, va[i], c.z);  // c2 + c3 a
@@ -438,13 +425,12 @@ logic_forward_narrow_kernel(const LayerArgs a, T* __restrict__ y, const int64_t 
         for (int i = 0; i < VEC; ++i) acc[i] = c0;
         if (active) {
             const int ns = st.ns[t];
-            const SlotRec<A>* rec = st.rec + t * K;
+            const int2* ab = st.ab + t * K;
+            const A4<A>* cf = st.cf + t * K;
 #pragma unroll 4
             for (int s = 0; s < ns; ++s) {
-                const SlotRec<A> r = rec[s];
-                const int2 pr = make_int2(r.a, r.b);
-                const float4 cg = kGatePoly[r.g];
-                const A4<A> c{r.p * (A)cg.y, r.p * (A)cg.z, r.p * (A)cg.w, (A)0};  // p*c1, p*c2, p*c3
+                const int2 pr = ab[s];
+                const A4<A> c = cf[s];
                 A va[VEC], vb[VEC];
                 gather<T, VEC>(x, pr.x, a.ldx, col, va);
                 gather<T, VEC>(x, pr.y, a.ldx, col, vb);
@@ -513,20 +499,20 @@ logic_backward_narrow_kernel(const LayerArgs a, const typename Acc<T>::type* __r
 #pragma unroll
             for (int i = 0; i < VEC; ++i) g[i] = 0;
         }
-        const SlotRec<A>* rec = st.rec + ts * K;
+        const int2* ab = st.ab + ts * K;
+        const A4<A>* cf = st.cf + ts * K;
+        const A* pp = st.p + ts * K;
         A pk[KT > 0 ? KT : 1];
 #pragma unroll(KT > 0 ? KT : 4)
         for (int s = 0; s < K; ++s) {
-            const SlotRec<A> r = rec[s];
-            const int2 pr = live ? make_int2(r.a, r.b) : make_int2(-1, -1);
-            const float4 cg = kGatePoly[r.g];
-            const A4<A> c{(A)cg.x, (A)cg.y, (A)cg.z, (A)cg.w};
+            const int2 pr = live ? ab[s] : make_int2(-1, -1);
+            const A4<A> c = cf[s];
             A va[VEC], vb[VEC];
             gather<T, VEC>(x, pr.x, a.ldx, col, va);
             gather<T, VEC>(x, pr.y, a.ldx, col, vb);
             A dot = 0;
             A da[VEC], db[VEC];
-            const A pw = r.p;
+            const A pw = pp[s];
 #pragma unroll
             for (int i = 0; i < VEC; ++i) {
                 const A dfdb = fma(c.w, va[i], c.z);
