@@ -751,14 +751,22 @@ class EntropyRowResampler:
         self.counter = {}
         self.iter = 0
 
+    #: on CUDA layers with fp32 logits, run the per-row monitor as one fused kernel per layer and read
+    #: the converged counts of all layers with a single host synchronisation per step
+    use_device_monitor = True
+
     @torch.no_grad()
     def step(self, iter: int, optimizer):
         self.iter = iter
         if self.iter < self.min_iters or self.iter > self.max_iters:
             return
-        for idx, layer in self.layers:
-            if self.only_unfrozen and getattr(layer, "is_frozen", False):
-                continue
+        active = [(idx, layer) for idx, layer in self.layers
+                  if not (self.only_unfrozen and getattr(layer, "is_frozen", False))]
+        if self.use_device_monitor and active and all(
+                l.weights.is_cuda and l.weights.dtype == torch.float32 for _, l in active):
+            self._step_device(active, optimizer)
+            return
+        for idx, layer in active:
             h = layer.weights_entropy().detach()
             assert h.dim() == 1
             if idx not in self.ema:
@@ -770,11 +778,40 @@ class EntropyRowResampler:
             cnt = self.counter[idx]
             self.counter[idx] = torch.where((h - old).abs() < self.eps, cnt + 1, torch.zeros_like(cnt))
             rows = (self.counter[idx] >= self.patience).nonzero(as_tuple=False).flatten()
-            if rows.numel() > 0:
-                weak, strong = layer.resample_connections(rows, **self.resample_kwargs)
-                changed = torch.logical_or(weak, strong)
-                self.reset_adam_state_for_mask(optimizer, layer.weights, changed[:, None].expand_as(layer.weights))
-                self.counter[idx][rows] = 0
+            self._resample(idx, layer, rows, optimizer)
+
+    def _resample(self, idx, layer, rows, optimizer):
+        if rows.numel() > 0:
+            weak, strong = layer.resample_connections(rows, **self.resample_kwargs)
+            changed = torch.logical_or(weak, strong)
+            self.reset_adam_state_for_mask(optimizer, layer.weights, changed[:, None].expand_as(layer.weights))
+            self.counter[idx][rows] = 0
+
+    def _step_device(self, active, optimizer):
+        dev = active[0][1].weights.device
+        counts = torch.zeros(len(active), dtype=torch.int32, device=dev)
+        pending = []
+        for i, (idx, layer) in enumerate(active):
+            w = layer.weights.detach()
+            if w.stride(-1) != 1 or w.stride(0) != w.shape[1]:
+                w = w.contiguous()
+            rows = w.shape[0]
+            first = idx not in self.ema
+            if first:
+                self.ema[idx] = torch.empty(rows, dtype=torch.float32, device=dev)
+                self.counter[idx] = torch.zeros(rows, dtype=torch.int32, device=dev)
+            flags = torch.empty(rows, dtype=torch.uint8, device=dev)
+            L.call("clb_entropy_monitor", L.ptr(w), rows, w.shape[1], float(self.ema_decay), float(self.eps),
+                   int(min(self.patience, 2**31 - 1)), int(first), L.ptr(self.ema[idx]), L.ptr(self.counter[idx]),
+                   L.ptr(flags), L.ptr(counts[i:i + 1]), L.stream(dev))
+            if not first:
+                pending.append((i, idx, layer, flags))
+        if not pending:
+            return
+        host_counts = counts.cpu()  # the one synchronisation of the step
+        for i, idx, layer, flags in pending:
+            if int(host_counts[i]) > 0:
+                self._resample(idx, layer, flags.nonzero(as_tuple=False).flatten(), optimizer)
 
     @torch.no_grad()
     def reset_adam_state_for_mask(self, optimizer, param, mask):

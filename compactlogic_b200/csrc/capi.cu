@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cmath>
 #include <string>
 
 #include "common.cuh"
@@ -232,6 +233,18 @@ int clb_pack_inputs(int dtype, const void* x, int64_t batch, int64_t features, i
         return fail(CLB_ERR_INVALID, "pack_inputs: bad sizes");
     if (batch * features > 0 && (!x || !out)) return fail(CLB_ERR_INVALID, "pack_inputs: null");
     return cuda_status(launch_pack_inputs(dtype, x, batch, features, ldx, out, ldw, S(stream)), "pack_inputs");
+}
+
+int clb_entropy_monitor(const float* logits, int64_t rows, int64_t K, float ema_decay, float eps, int patience,
+                        int first, float* ema, int32_t* counter, uint8_t* converged, int32_t* n_converged,
+                        clb_stream_t stream) {
+    if (rows < 0 || K < 1) return fail(CLB_ERR_INVALID, "entropy_monitor: bad sizes");
+    if (rows > 0 && (!logits || !ema || !counter || !converged || !n_converged))
+        return fail(CLB_ERR_INVALID, "entropy_monitor: null");
+    const float inv_log_k = K > 1 ? (float)(1.0 / log((double)K)) : 0.f;
+    return cuda_status(launch_entropy_monitor(logits, rows, (int)K, inv_log_k, ema, counter, first, ema_decay, eps,
+                                              patience, converged, n_converged, S(stream)),
+                       "entropy_monitor");
 }
 
 int clb_pack_thresholds(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, int nthr,

@@ -94,6 +94,11 @@ cudaError_t launch_packed_layer_count(const uint64_t* x, int64_t ldx, int64_t nw
                                       cudaStream_t s);
 size_t packed_count_workspace_bytes(int64_t k, int64_t class_size, int64_t nwords);
 
+// Fused entropy / EMA / patience monitor of EntropyRowResampler (hooks.cu).
+cudaError_t launch_entropy_monitor(const float* logits, int64_t rows, int K, float inv_log_k, float* ema,
+                                   int32_t* counter, int first, float decay, float eps, int patience,
+                                   uint8_t* converged, int32_t* n_converged, cudaStream_t s);
+
 // Error / launch bookkeeping of the C ABI (capi.cu), for entry points defined in other files.
 int set_error(int code, const char* msg);
 void count_launches(int n);

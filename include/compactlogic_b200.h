@@ -222,6 +222,17 @@ int clb_transpose(int elem_bytes, const void* src, int64_t rows, int64_t cols, i
                   int64_t ld_dst, clb_stream_t stream);
 int clb_cast(int src_dtype, const void* src, int dst_dtype, void* dst, int64_t n, clb_stream_t stream);
 
+/* ---- training hooks ---- */
+
+/* One step of EntropyRowResampler's per-row monitor for one layer (compactlogic/compactlogic.py:1113-1150):
+ * h = normalised entropy of softmax(logits[r]) (weights_entropy, compactlogic.py:370-385); first call
+ * (first != 0): ema = h, counter = 0; later: ema = decay*ema + (1-decay)*h, counter = |h - ema_old| < eps ?
+ * counter + 1 : 0, converged[r] = counter >= patience.  n_converged (device int, zero it first) receives
+ * the number of converged rows.  logits fp32 [rows, K]; ema fp32 / counter int32 / converged uint8 [rows]. */
+int clb_entropy_monitor(const float* logits, int64_t rows, int64_t K, float ema_decay, float eps, int patience,
+                        int first, float* ema, int32_t* counter, uint8_t* converged, int32_t* n_converged,
+                        clb_stream_t stream);
+
 /* ---- bit-packed discrete inference (uint64 words, bit i of word w = sample 64 w + i) ---- */
 
 /* x [batch, features] sample-major with values in {0,1} (bit = x > 0.5) -> out [features, ldw]. */
