@@ -15,7 +15,7 @@ from typing import List, Optional
 import torch
 
 from . import _lib as L
-from .compactlogic import ConvLayer, GroupSum, LogicLayer
+from .compactlogic import GroupSum, LogicLayer
 
 
 class _Frozen:

@@ -230,3 +230,41 @@ def test_narrow_chunks_opt_in(dtype, in_dim, out, K, B, lpn):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-3000:]
+
+
+def test_reference_autograd_bridges():
+    """LogicLayerCudaFunction / ConvLayerCudaFunction (the reference bridges, compactlogic.py:474-508,
+    838-867) driven exactly as the reference's forward_cuda drives them give the native layers' results."""
+    torch.manual_seed(6)
+    layer = cl.LogicLayer(50, 60, num_gates=16).cuda()
+    x = torch.rand(12, 50, device="cuda")
+    xr = x.clone().requires_grad_(True)
+    w = torch.nn.functional.softmax(layer.weights, dim=-1)
+    y_ref = cl.LogicLayerCudaFunction.apply(xr.t().contiguous(), layer.indices[0], layer.indices[1], w,
+                                            layer.gate_sequence, layer.given_x_indices_of_y_start,
+                                            layer.given_x_indices_of_y, layer.given_x_indices_of_gate).t()
+    gy = torch.randn_like(y_ref)
+    y_ref.backward(gy)
+    g_ref, gx_ref = layer.weights.grad.clone(), xr.grad.clone()
+    layer.weights.grad = None
+    xn = x.clone().requires_grad_(True)
+    y = layer(xn)
+    y.backward(gy)
+    torch.testing.assert_close(y, y_ref, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(layer.weights.grad, g_ref, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(xn.grad, gx_ref, rtol=1e-5, atol=1e-6)
+
+    conv = cl.ConvLayer((4, 6, 6), 1, 8, 3, 2, num_gates=8).cuda()
+    xc = torch.rand(3, 4, 6, 6, device="cuda", requires_grad=True)
+    wc = torch.nn.functional.softmax(conv.weights, dim=-1)
+    yc_ref = cl.ConvLayerCudaFunction.apply(xc, conv.offsets_ch, conv.offsets_h, conv.offsets_w, wc,
+                                            conv.gate_sequence, conv.stride, conv.padding, conv.ks)
+    gyc = torch.randn_like(yc_ref)
+    yc_ref.backward(gyc)
+    gc_ref, gxc_ref = conv.weights.grad.clone(), xc.grad.clone()
+    conv.weights.grad, xc.grad = None, None
+    yc = conv(xc)
+    yc.backward(gyc)
+    torch.testing.assert_close(yc, yc_ref, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(conv.weights.grad, gc_ref, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(xc.grad, gxc_ref, rtol=1e-5, atol=1e-6)
