@@ -13,10 +13,10 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libcompactlogic_b200.so")
 
 CLB_OK, CLB_ERR_INVALID, CLB_ERR_DTYPE, CLB_ERR_INDEX, CLB_ERR_CUDA, CLB_ERR_WORKSPACE, CLB_ERR_DIVISIBILITY = range(7)
-CLB_F32, CLB_F64, CLB_BF16 = 0, 1, 2
+CLB_F32, CLB_F64, CLB_BF16, CLB_F16 = 0, 1, 2, 3
 W_LOGITS, W_PROBS, W_SELECT = 0, 1, 2
 
-_DTYPES = {torch.float32: CLB_F32, torch.float64: CLB_F64, torch.bfloat16: CLB_BF16}
+_DTYPES = {torch.float32: CLB_F32, torch.float64: CLB_F64, torch.bfloat16: CLB_BF16, torch.float16: CLB_F16}
 
 _i64, _int, _p, _sz, _dbl = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_double
 
@@ -25,7 +25,7 @@ _SIGS = {
     "clb_last_error": (ctypes.c_char_p, []),
     "clb_abi_version": (_int, []),
     "clb_launch_count": (ctypes.c_longlong, []),
-    "clb_difflogic_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
+    "clb_difflogic_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _int]),
     "clb_difflogic_forward": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _sz, _p]),
     "clb_difflogic_backward_w": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _sz, _p]),
     "clb_difflogic_backward_w_noalloc": (_int, [_int, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p]),
@@ -112,7 +112,7 @@ def dtype_code(dt: torch.dtype) -> int:
     try:
         return _DTYPES[dt]
     except KeyError:
-        raise RuntimeError(f"compactlogic_b200: unsupported dtype {dt} (float32, float64, bfloat16)") from None
+        raise RuntimeError(f"compactlogic_b200: unsupported dtype {dt} (float32, float64, bfloat16, float16)") from None
 
 
 def acc_dtype(dt: torch.dtype) -> torch.dtype:

@@ -91,7 +91,7 @@ class LogicLayer(torch.nn.Module):
             k, tau = self._fused_groupsum
             acc = LogicGroupSumFn.apply(xt, w, spec, k, _group_size(self.out_dim, k), in_slot)
             return acc.transpose(0, 1) / tau
-        out_slot = GradSlot() if xt.dtype == torch.bfloat16 else None
+        out_slot = GradSlot() if xt.dtype in (torch.bfloat16, torch.float16) else None
         y = LogicLayerFn.apply(xt, w, spec, in_slot, out_slot).transpose(0, 1)
         if out_slot is not None:
             y._clb_slot = out_slot
@@ -462,7 +462,7 @@ class ConvLayer(LogicLayer):
         in_slot = getattr(x, "_clb_slot", None)
         xt = self._to_feature_major(x)
         spec = self._layer_spec(xt.device)
-        out_slot = GradSlot() if xt.dtype == torch.bfloat16 else None
+        out_slot = GradSlot() if xt.dtype in (torch.bfloat16, torch.float16) else None
         y = self._to_public(LogicLayerFn.apply(xt, self._weights_for(xt.dtype), spec, in_slot, out_slot))
         if out_slot is not None:
             y._clb_slot = out_slot

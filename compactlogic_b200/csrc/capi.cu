@@ -37,10 +37,11 @@ int cuda_status(cudaError_t e, const char* where, int kernels = 1) {
     return CLB_OK;
 }
 
-size_t esize(int dtype) { return dtype == CLB_F64 ? 8 : dtype == CLB_BF16 ? 2 : 4; }
+size_t esize(int dtype) { return dtype == CLB_F64 ? 8 : (dtype == CLB_BF16 || dtype == CLB_F16) ? 2 : 4; }
 size_t acc_size(int dtype) { return dtype == CLB_F64 ? 8 : 4; }
-bool dtype_ok(int dtype) { return dtype == CLB_F32 || dtype == CLB_F64 || dtype == CLB_BF16; }
-bool ref_dtype_ok(int dtype) { return dtype == CLB_F32 || dtype == CLB_F64; }
+bool dtype_ok(int dtype) { return dtype == CLB_F32 || dtype == CLB_F64 || dtype == CLB_BF16 || dtype == CLB_F16; }
+bool ref_dtype_ok(int dtype) { return dtype == CLB_F32 || dtype == CLB_F64 || dtype == CLB_F16; }
+bool ref_conv_dtype_ok(int dtype) { return dtype == CLB_F32 || dtype == CLB_F64; }
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 cudaStream_t S(clb_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -306,15 +307,46 @@ int clb_packed_count(const uint64_t* words, int64_t rows, int64_t nwords, int64_
 // ----------------------------------------------------------------------------------------------
 // reference-mirroring entry points
 // ----------------------------------------------------------------------------------------------
-size_t clb_difflogic_workspace_bytes(int64_t out_dim, int64_t K, int64_t batch, int dtype) {
+size_t clb_difflogic_workspace_bytes(int64_t in_dim, int64_t out_dim, int64_t K, int64_t batch, int dtype) {
     const int64_t chunks = (batch + 31) / 32;  // upper bound (scalar path)
-    return align256((size_t)out_dim * K * 8) + align256(4) + align256((size_t)chunks * out_dim * K * acc_size(dtype)) + 256;
+    size_t b = align256((size_t)out_dim * K * 8) + align256(4) + align256((size_t)chunks * out_dim * K * acc_size(dtype)) + 256;
+    if (dtype == CLB_F16)  // fp32 copies of w, grad_y and of the result
+        b += align256((size_t)out_dim * K * 4) + align256((size_t)out_dim * batch * 4) +
+             align256((size_t)std::max(in_dim * batch, out_dim * K) * 4);
+    return b;
 }
+
+namespace {
+// fp16 entry points: fp32 staging of the probabilities, grad_y and the result in the workspace.
+struct HalfStage {
+    void* w = nullptr;
+    void* gy = nullptr;
+    void* out = nullptr;
+};
+
+int half_stage(int dtype, Carve& cv, int64_t in_dim, int64_t out_dim, int64_t K, int64_t batch, const void* w,
+               const void* gy, HalfStage& h, cudaStream_t s) {
+    if (dtype != CLB_F16) return CLB_OK;
+    h.w = cv.take((size_t)out_dim * K * 4);
+    h.gy = cv.take((size_t)out_dim * batch * 4);
+    h.out = cv.take((size_t)std::max(in_dim * batch, out_dim * K) * 4);
+    if (!h.out) return fail(CLB_ERR_WORKSPACE, "workspace too small for the fp16 staging");
+    if (w) {
+        cudaError_t e = launch_cast(CLB_F16, w, CLB_F32, h.w, out_dim * K, s);
+        if (e != cudaSuccess) return cuda_status(e, "cast w");
+    }
+    if (gy) {
+        cudaError_t e = launch_cast(CLB_F16, gy, CLB_F32, h.gy, out_dim * batch, s);
+        if (e != cudaSuccess) return cuda_status(e, "cast grad_y");
+    }
+    return CLB_OK;
+}
+}  // namespace
 
 static int dense_common(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a, const int64_t* b,
                         int64_t out_dim, int64_t K, void* ws, size_t ws_bytes, Carve& cv, int32_t*& slots,
                         cudaStream_t s) {
-    if (!ref_dtype_ok(dtype)) return fail(CLB_ERR_DTYPE, "reference API supports fp32/fp64 only");
+    if (!ref_dtype_ok(dtype)) return fail(CLB_ERR_DTYPE, "reference dense API supports fp32/fp64/fp16 only");
     if (in_dim < 0 || batch < 0 || out_dim < 0 || K < 1 || K > 256) return fail(CLB_ERR_INVALID, "bad sizes");
     if ((in_dim * batch > 0 && !x) || (out_dim * K > 0 && (!a || !b))) return fail(CLB_ERR_INVALID, "null pointer");
     cv = Carve{reinterpret_cast<char*>(ws), ws_bytes};
@@ -331,6 +363,9 @@ int clb_difflogic_forward(int dtype, const void* x, int64_t in_dim, int64_t batc
     int32_t* slots = nullptr;
     int st = dense_common(dtype, x, in_dim, batch, a, b, out_dim, K, workspace, workspace_bytes, cv, slots, S(stream));
     if (st) return st;
+    HalfStage hs;
+    if ((st = half_stage(dtype, cv, in_dim, out_dim, K, batch, w, nullptr, hs, S(stream)))) return st;
+    if (dtype == CLB_F16) w = hs.w;
     return clb_logic_forward(dtype, x, batch, batch, in_dim, slots, out_dim, K, 1, CLB_W_PROBS, w, gate_seq, nullptr, 0, y,
                              batch, nullptr, 0, 0, 0, stream);
 }
@@ -353,15 +388,20 @@ int clb_difflogic_backward_w(int dtype, const void* x, int64_t in_dim, int64_t b
     int32_t* slots = nullptr;
     int st = dense_common(dtype, x, in_dim, batch, a, b, out_dim, K, workspace, workspace_bytes, cv, slots, S(stream));
     if (st) return st;
-    const int64_t chunks = clb_logic_backward_chunks(dtype, x, batch, batch, in_dim, grad_y, batch, nullptr, 0, nullptr, 0);
+    HalfStage hs;
+    if ((st = half_stage(dtype, cv, in_dim, out_dim, K, batch, nullptr, grad_y, hs, S(stream)))) return st;
+    const void* gy = dtype == CLB_F16 ? hs.gy : grad_y;
+    void* gw = dtype == CLB_F16 ? hs.out : grad_w;
+    const int64_t chunks = clb_logic_backward_chunks(dtype, x, batch, batch, in_dim, gy, batch, nullptr, 0, nullptr, 0);
     void* part = cv.take((size_t)std::max<int64_t>(chunks, 1) * out_dim * K * acc_size(dtype));
     if (!part) return fail(CLB_ERR_WORKSPACE, "workspace too small for partials");
     // d loss / d prob does not depend on the probabilities: no weights needed
-    st = clb_logic_backward(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_PROBS, nullptr, gate_seq, 0, grad_y,
-                            batch, nullptr, 0, 0, 0, 0.0, nullptr, 0, 0, in_dim, part, chunks, stream);
+    st = clb_logic_backward(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_PROBS, nullptr, gate_seq, 0, gy, batch,
+                            nullptr, 0, 0, 0, 0.0, nullptr, 0, 0, in_dim, part, chunks, stream);
     if (st) return st;
-    return clb_logic_grad_finalize(dtype, part, batch > 0 ? chunks : 0, out_dim, K, 1, CLB_W_PROBS, nullptr, grad_w,
-                                   stream);
+    st = clb_logic_grad_finalize(dtype, part, batch > 0 ? chunks : 0, out_dim, K, 1, CLB_W_PROBS, nullptr, gw, stream);
+    if (st || dtype != CLB_F16) return st;
+    return cuda_status(launch_cast(CLB_F32, gw, CLB_F16, grad_w, out_dim * K, S(stream)), "cast grad_w");
 }
 
 int clb_difflogic_backward_x_atomic(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
@@ -373,8 +413,14 @@ int clb_difflogic_backward_x_atomic(int dtype, const void* x, int64_t in_dim, in
     int st = dense_common(dtype, x, in_dim, batch, a, b, out_dim, K, workspace, workspace_bytes, cv, slots, S(stream));
     if (st) return st;
     if (!grad_x && in_dim * batch > 0) return fail(CLB_ERR_INVALID, "null grad_x");
-    return clb_logic_backward(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_PROBS, w, gate_seq, 0, grad_y, batch,
-                              nullptr, 0, 0, 0, 0.0, grad_x, batch, 1, in_dim, nullptr, 0, stream);
+    HalfStage hs;
+    if ((st = half_stage(dtype, cv, in_dim, out_dim, K, batch, w, grad_y, hs, S(stream)))) return st;
+    const bool h = dtype == CLB_F16;
+    st = clb_logic_backward(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_PROBS, h ? hs.w : w, gate_seq, 0,
+                            h ? hs.gy : grad_y, batch, nullptr, 0, 0, 0, 0.0, h ? hs.out : grad_x, batch, 1, in_dim,
+                            nullptr, 0, stream);
+    if (st || !h) return st;
+    return cuda_status(launch_cast(CLB_F32, hs.out, CLB_F16, grad_x, in_dim * batch, S(stream)), "cast grad_x");
 }
 
 int clb_difflogic_backward_x(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
@@ -388,9 +434,16 @@ int clb_difflogic_backward_x(int dtype, const void* x, int64_t in_dim, int64_t b
     if (in_dim * batch == 0) return CLB_OK;
     if (!grad_x || !starts || (out_dim > 0 && (!ys || !gate_codes || !w || !gate_seq || !grad_y)))
         return fail(CLB_ERR_INVALID, "backward_x: null pointer");
-    const LayerArgs la = layer(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_PROBS, w, gate_seq, nullptr, false);
-    return cuda_status(launch_backward_x_csr(la, grad_y, batch, in_dim, starts, ys, gate_codes, grad_x, batch, S(stream)),
-                       "backward_x_csr");
+    HalfStage hs;
+    if ((st = half_stage(dtype, cv, in_dim, out_dim, K, batch, w, grad_y, hs, S(stream)))) return st;
+    const bool h = dtype == CLB_F16;
+    const LayerArgs la = layer(dtype, x, batch, batch, slots, out_dim, K, 1, CLB_W_PROBS, h ? hs.w : w, gate_seq, nullptr,
+                               false);
+    st = cuda_status(launch_backward_x_csr(la, h ? hs.gy : grad_y, batch, in_dim, starts, ys, gate_codes,
+                                           h ? hs.out : grad_x, batch, S(stream)),
+                     "backward_x_csr");
+    if (st || !h) return st;
+    return cuda_status(launch_cast(CLB_F32, hs.out, CLB_F16, grad_x, in_dim * batch, S(stream)), "cast grad_x");
 }
 
 int clb_tensor_packbits(const uint8_t* t, int64_t rows, int64_t cols, int bit_count, void* out, int64_t* pad_len_host,
@@ -447,7 +500,7 @@ struct ConvWs {
 int conv_common(int dtype, const void* x, int64_t n, int64_t c_in, int64_t h_in, int64_t w_in, const int32_t* och,
                 const int8_t* oh, const int8_t* ow, int64_t c_out, int64_t h_out, int64_t w_out, int64_t K, int stride,
                 void* ws, size_t ws_bytes, ConvWs& w, cudaStream_t s) {
-    if (!ref_dtype_ok(dtype)) return fail(CLB_ERR_DTYPE, "reference conv API supports fp32/fp64 only");
+    if (!ref_conv_dtype_ok(dtype)) return fail(CLB_ERR_DTYPE, "reference conv API supports fp32/fp64 only");
     if (n < 0 || c_in < 1 || h_in < 1 || w_in < 1 || c_out < 0 || h_out <= 0 || w_out <= 0 || K < 1 || K > 256 ||
         stride < 1)
         return fail(CLB_ERR_INVALID, "Invalid output shape: h_out=%lld, w_out=%lld", (long long)h_out, (long long)w_out);

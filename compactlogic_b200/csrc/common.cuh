@@ -8,6 +8,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "../../include/compactlogic_b200.h"
@@ -24,10 +25,12 @@ template <> struct Acc<double> { using type = double; };
 __device__ __forceinline__ float to_acc(float v) { return v; }
 __device__ __forceinline__ double to_acc(double v) { return v; }
 __device__ __forceinline__ float to_acc(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_acc(__half v) { return __half2float(v); }
 
 template <typename T> __device__ __forceinline__ T from_acc(float v);
 template <> __device__ __forceinline__ float from_acc<float>(float v) { return v; }
 template <> __device__ __forceinline__ __nv_bfloat16 from_acc<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half from_acc<__half>(float v) { return __float2half_rn(v); }
 template <typename T> __device__ __forceinline__ T from_acc(double v) { return (T)v; }
 
 // VEC consecutive elements as one aligned vector of at most 16 bytes.

@@ -1024,6 +1024,7 @@ cudaError_t launch_logic_forward(const LayerArgs& a, void* y, int64_t ldy, const
         case CLB_F32: return fwd_t<float>(a, y, ldy, gs, s);
         case CLB_F64: return fwd_t<double>(a, y, ldy, gs, s);
         case CLB_BF16: return fwd_t<__nv_bfloat16>(a, y, ldy, gs, s);
+        case CLB_F16: return fwd_t<__half>(a, y, ldy, gs, s);
     }
     return cudaErrorInvalidValue;
 }
@@ -1034,6 +1035,7 @@ cudaError_t launch_logic_backward(const LayerArgs& a, const void* gy, int64_t ld
         case CLB_F32: return bwd_t<float>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
         case CLB_F64: return bwd_t<double>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
         case CLB_BF16: return bwd_t<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
+        case CLB_F16: return bwd_t<__half>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
     }
     return cudaErrorInvalidValue;
 }
@@ -1071,6 +1073,11 @@ int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void*
             v = vec ? vmax<__nv_bfloat16>() : 1;
             lpn = bwd_lpn<__nv_bfloat16>(a, vec, v, gx);
             break;
+        case CLB_F16:
+            vec = bwd_vec<__half>(a, gy, ldgy, gs, gx, ldgx);
+            v = vec ? vmax<__half>() : 1;
+            lpn = bwd_lpn<__half>(a, vec, v, gx);
+            break;
         default: return -1;
     }
     return ceil_div64(ncols, lpn * v);
@@ -1106,6 +1113,7 @@ cudaError_t launch_backward_x_csr(const LayerArgs& a, const void* gy, int64_t ld
         case CLB_F32: return csr_t<float>(a, gy, ldgy, in_dim, starts, ys, codes, gx, ldgx, s);
         case CLB_F64: return csr_t<double>(a, gy, ldgy, in_dim, starts, ys, codes, gx, ldgx, s);
         case CLB_BF16: return csr_t<__nv_bfloat16>(a, gy, ldgy, in_dim, starts, ys, codes, gx, ldgx, s);
+        case CLB_F16: return csr_t<__half>(a, gy, ldgy, in_dim, starts, ys, codes, gx, ldgx, s);
     }
     return cudaErrorInvalidValue;
 }
@@ -1152,6 +1160,10 @@ cudaError_t launch_cast(int src_dtype, const void* src, int dst_dtype, void* dst
         cast_kernel<float, __nv_bfloat16><<<blocks, 256, 0, s>>>((const float*)src, (__nv_bfloat16*)dst, n);
     else if (src_dtype == CLB_BF16 && dst_dtype == CLB_F32)
         cast_kernel<__nv_bfloat16, float><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)src, (float*)dst, n);
+    else if (src_dtype == CLB_F32 && dst_dtype == CLB_F16)
+        cast_kernel<float, __half><<<blocks, 256, 0, s>>>((const float*)src, (__half*)dst, n);
+    else if (src_dtype == CLB_F16 && dst_dtype == CLB_F32)
+        cast_kernel<__half, float><<<blocks, 256, 0, s>>>((const __half*)src, (float*)dst, n);
     else
         return cudaErrorInvalidValue;
     return cudaGetLastError();

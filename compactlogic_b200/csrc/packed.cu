@@ -447,6 +447,7 @@ cudaError_t launch_pack_inputs(int dtype, const void* x, int64_t batch, int64_t 
         case CLB_F32: pack_inputs_kernel<float><<<grid, block, 0, s>>>((const float*)x, batch, features, ldx, out, ldw); break;
         case CLB_F64: pack_inputs_kernel<double><<<grid, block, 0, s>>>((const double*)x, batch, features, ldx, out, ldw); break;
         case CLB_BF16: pack_inputs_kernel<__nv_bfloat16><<<grid, block, 0, s>>>((const __nv_bfloat16*)x, batch, features, ldx, out, ldw); break;
+        case CLB_F16: pack_inputs_kernel<__half><<<grid, block, 0, s>>>((const __half*)x, batch, features, ldx, out, ldw); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -461,6 +462,7 @@ cudaError_t launch_pack_thresholds(int dtype, const void* x, int64_t batch, int6
         case CLB_F32: pack_thresholds_kernel<float><<<grid, block, 0, s>>>((const float*)x, batch, features, ldx, nthr, out, ldw); break;
         case CLB_F64: pack_thresholds_kernel<double><<<grid, block, 0, s>>>((const double*)x, batch, features, ldx, nthr, out, ldw); break;
         case CLB_BF16: pack_thresholds_kernel<__nv_bfloat16><<<grid, block, 0, s>>>((const __nv_bfloat16*)x, batch, features, ldx, nthr, out, ldw); break;
+        case CLB_F16: pack_thresholds_kernel<__half><<<grid, block, 0, s>>>((const __half*)x, batch, features, ldx, nthr, out, ldw); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -3,7 +3,7 @@
 Same function names, argument order, layouts, dtypes and results; each call goes through the C ABI
 (clb_difflogic_*, clb_tensor_packbits, clb_groupbitsum).  Inputs must be contiguous CUDA tensors
 (the reference's CHECK_INPUT, compactlogic/cuda/utils.cuh:10-14); outputs are allocated here, as in
-the reference.  fp32 and fp64 activations are supported.
+the reference.  fp32, fp64 and fp16 activations are supported, as in the reference.
 """
 import ctypes
 
@@ -23,8 +23,8 @@ def _check(**tensors):
             raise RuntimeError(f"{name} must be contiguous")
 
 
-def _ws(out_dim, K, batch, dtype, device):
-    n = int(L.lib().clb_difflogic_workspace_bytes(out_dim, K, batch, L.dtype_code(dtype)))
+def _ws(in_dim, out_dim, K, batch, dtype, device):
+    n = int(L.lib().clb_difflogic_workspace_bytes(in_dim, out_dim, K, batch, L.dtype_code(dtype)))
     return torch.empty(n, dtype=torch.uint8, device=device)
 
 
@@ -33,7 +33,7 @@ def forward(x, a, b, w, gate_seq):
     _check(x=x, a=a, b=b, w=w, gate_seq=gate_seq)
     out_dim, K = w.shape
     y = torch.empty(out_dim, x.shape[1], dtype=x.dtype, device=x.device)
-    ws = _ws(out_dim, K, x.shape[1], x.dtype, x.device)
+    ws = _ws(x.shape[0], out_dim, K, x.shape[1], x.dtype, x.device)
     L.call("clb_difflogic_forward", L.dtype_code(x.dtype), L.ptr(x), x.shape[0], x.shape[1], L.ptr(a), L.ptr(b),
            L.ptr(w), L.ptr(gate_seq), out_dim, K, L.ptr(y), L.ptr(ws), ws.numel(), L.stream(x.device))
     return y
@@ -44,7 +44,7 @@ def backward_w(x, a, b, gate_seq, grad_y):
     _check(x=x, a=a, b=b, gate_seq=gate_seq, grad_y=grad_y)
     out_dim, K = a.shape
     gw = torch.empty(out_dim, K, dtype=x.dtype, device=x.device)
-    ws = _ws(out_dim, K, x.shape[1], x.dtype, x.device)
+    ws = _ws(x.shape[0], out_dim, K, x.shape[1], x.dtype, x.device)
     L.call("clb_difflogic_backward_w", L.dtype_code(x.dtype), L.ptr(x), x.shape[0], x.shape[1], L.ptr(a), L.ptr(b),
            L.ptr(gate_seq), L.ptr(grad_y), out_dim, K, L.ptr(gw), L.ptr(ws), ws.numel(), L.stream(x.device))
     return gw
@@ -57,7 +57,7 @@ def backward_x(x, a, b, w, gate_seq, grad_y, given_x_indices_of_y_start, given_x
            given_x_indices_of_y=given_x_indices_of_y, given_x_types_of_gate=given_x_types_of_gate)
     out_dim, K = w.shape
     gx = torch.empty_like(x)
-    ws = _ws(out_dim, K, x.shape[1], x.dtype, x.device)
+    ws = _ws(x.shape[0], out_dim, K, x.shape[1], x.dtype, x.device)
     L.call("clb_difflogic_backward_x", L.dtype_code(x.dtype), L.ptr(x), x.shape[0], x.shape[1], L.ptr(a), L.ptr(b),
            L.ptr(w), L.ptr(gate_seq), L.ptr(grad_y), L.ptr(given_x_indices_of_y_start), L.ptr(given_x_indices_of_y),
            L.ptr(given_x_types_of_gate), out_dim, K, L.ptr(gx), L.ptr(ws), ws.numel(), L.stream(x.device))
@@ -69,7 +69,7 @@ def backward_x_atomicAdd(x, a, b, w, gate_seq, grad_y):
     _check(x=x, a=a, b=b, w=w, gate_seq=gate_seq, grad_y=grad_y)
     out_dim, K = w.shape
     gx = torch.empty_like(x)
-    ws = _ws(out_dim, K, x.shape[1], x.dtype, x.device)
+    ws = _ws(x.shape[0], out_dim, K, x.shape[1], x.dtype, x.device)
     L.call("clb_difflogic_backward_x_atomic", L.dtype_code(x.dtype), L.ptr(x), x.shape[0], x.shape[1], L.ptr(a),
            L.ptr(b), L.ptr(w), L.ptr(gate_seq), L.ptr(grad_y), out_dim, K, L.ptr(gx), L.ptr(ws), ws.numel(),
            L.stream(x.device))
@@ -81,7 +81,7 @@ def eval(x, a, b, w, gate_seq):  # noqa: A001 - the reference's name
     _check(x=x, a=a, b=b, w=w, gate_seq=gate_seq)
     out_dim, K = a.shape
     y = torch.empty(out_dim, x.shape[1], dtype=x.dtype, device=x.device)
-    ws = _ws(out_dim, K, x.shape[1], x.dtype, x.device)
+    ws = _ws(x.shape[0], out_dim, K, x.shape[1], x.dtype, x.device)
     L.call("clb_difflogic_eval", L.dtype_code(x.dtype), L.ptr(x), x.shape[0], x.shape[1], L.ptr(a), L.ptr(b),
            L.ptr(w), L.ptr(gate_seq), out_dim, K, L.ptr(y), L.ptr(ws), ws.numel(), L.stream(x.device))
     return y

@@ -126,7 +126,7 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
 
 
 class GradSlot:
-    """fp32 gradient hand-over between two logic layers whose activations are low precision (bf16).
+    """fp32 gradient hand-over between two logic layers whose activations are low precision (bf16 / fp16).
 
     Autograd casts a gradient to the dtype of the tensor it belongs to, which would round every
     inter-layer gradient to bf16.  A producing layer attaches a slot to its output; a logic layer that

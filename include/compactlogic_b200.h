@@ -45,7 +45,7 @@ enum clb_status {
     CLB_ERR_DIVISIBILITY = 6  /* groupbitsum: rows not divisible by k (reference raises ValueError) */
 };
 
-enum clb_dtype { CLB_F32 = 0, CLB_F64 = 1, CLB_BF16 = 2 };
+enum clb_dtype { CLB_F32 = 0, CLB_F64 = 1, CLB_BF16 = 2, CLB_F16 = 3 };  /* fp16 and bf16 compute in fp32 */
 
 /* How a layer's per-row weights are interpreted. */
 enum clb_weight_mode {
@@ -60,14 +60,16 @@ int clb_abi_version(void);
 long long clb_launch_count(void);
 
 /* ============================== 1. reference-mirroring entry points ==============================
- * Dtypes: the reference dispatches fp32/fp64(/fp16) for dense and fp32/fp64 for conv; here fp32 and
- * fp64 are accepted (fp16 is not).  Indices a, b are int64 [out_dim, K] (the two halves of the
- * layer's `indices` buffer), gate_seq uint8 [out_dim, K], w [out_dim, K] in the activation dtype.
+ * Dtypes: as the reference — fp32 / fp64 / fp16 for the dense entry points
+ * (AT_DISPATCH_FLOATING_TYPES_AND_HALF, difflogic_kernel.cu:222), fp32 / fp64 for conv.  fp16 computes in
+ * fp32 and its fp32 copies of w / grad_y / results live in the workspace.  Indices a, b are int64
+ * [out_dim, K] (the two halves of the layer's `indices` buffer), gate_seq uint8 [out_dim, K], w [out_dim, K]
+ * and grad tensors in the activation dtype.
  */
 
 /* Replaces difflogic_cuda.forward(x, a, b, w, gate_seq) -> y  (compactlogic/cuda/difflogic.cpp:61-66,
  * compactlogic/cuda/difflogic_kernel.cu:197-236).  x [in_dim, batch], y [out_dim, batch]. */
-size_t clb_difflogic_workspace_bytes(int64_t out_dim, int64_t K, int64_t batch, int dtype);
+size_t clb_difflogic_workspace_bytes(int64_t in_dim, int64_t out_dim, int64_t K, int64_t batch, int dtype);
 int clb_difflogic_forward(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
                           const int64_t* b, const void* w, const uint8_t* gate_seq, int64_t out_dim, int64_t K,
                           void* y, void* workspace, size_t workspace_bytes, clb_stream_t stream);

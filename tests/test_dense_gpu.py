@@ -268,3 +268,44 @@ def test_reference_autograd_bridges():
     torch.testing.assert_close(yc, yc_ref, rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(conv.weights.grad, gc_ref, rtol=1e-5, atol=1e-5)
     torch.testing.assert_close(xc.grad, gxc_ref, rtol=1e-5, atol=1e-6)
+
+
+def test_fp16_reference_api_and_layers():
+    """fp16 activations (the reference dense kernels dispatch half, difflogic_kernel.cu:222): the
+    reference-API shims and the native layers, against the oracle on fp16-rounded inputs (2e-3)."""
+    in_dim, out, K, B = 64, 80, 16, 48
+    x, a, b, logits, g, gy = rand_dense(21, in_dim, out, K, B)
+    h = lambda v: cuda(v, torch.float16)
+    r = lambda t: t.double().cpu().numpy()
+    xh, ph, gyh = h(x), h(O.softmax(logits)), h(gy)
+    xr, pr, gyr = r(xh), r(ph), r(gyh)
+    at, bt, gt = cuda(a), cuda(b), cuda(g)
+    y = difflogic_cuda.forward(xh, at, bt, ph, gt)
+    assert y.dtype == torch.float16
+    assert_close(y, O.dense_forward(xr, a, b, pr, g), 2e-3, "fp16 forward")
+    assert_close(difflogic_cuda.backward_w(xh, at, bt, gt, gyh), O.dense_backward_w(xr, a, b, g, gyr), 2e-3, "fp16 gw")
+    starts, ys, codes = O.inverse_index(a, b, in_dim)
+    gx_ref = O.dense_backward_x(xr, a, b, pr, g, gyr)
+    assert_close(difflogic_cuda.backward_x(xh, at, bt, ph, gt, gyh, cuda(starts), cuda(ys), cuda(codes)), gx_ref, 2e-3,
+                 "fp16 gx csr")
+    assert_close(difflogic_cuda.backward_x_atomicAdd(xh, at, bt, ph, gt, gyh), gx_ref, 2e-3, "fp16 gx atomic")
+    sel = O.argmax_first(logits)
+    xb = (x > 0.5).astype(np.float64)
+    np.testing.assert_array_equal(difflogic_cuda.eval(h(xb), at, bt, cuda(sel), gt).cpu().numpy(),
+                                  O.dense_eval(xb, a, b, sel, g))
+    # native layers with fp16 activations keep fp32 gradients between layers
+    torch.manual_seed(2)
+    layers = [cl.LogicLayer(64, 128, num_gates=8), cl.LogicLayer(128, 100, num_gates=8)]
+    model = cl.fuse_groupsum(torch.nn.Sequential(*layers, cl.GroupSum(5, 2.0))).cuda()
+    xin = (torch.rand(32, 64) < 0.5).float()
+    out = model(xin.cuda().half())
+    out.sum().backward()
+    tabs = [(m.indices.cpu().numpy(), m.gate_sequence.cpu().numpy(), O.softmax(m.weights.detach().cpu().numpy()))
+            for m in layers]
+    h1 = r(cuda(O.dense_forward(xin.numpy().T.astype(np.float64), tabs[0][0][0], tabs[0][0][1], tabs[0][2],
+                                tabs[0][1]), torch.float16))
+    lg = O.group_sum(O.dense_forward(h1, tabs[1][0][0], tabs[1][0][1], tabs[1][2], tabs[1][1]).T, 5, 2.0)
+    assert_close(out, lg, 2e-3, "fp16 model")
+    gy2 = O.group_sum_backward(np.ones_like(lg), 100, 5, 2.0).T
+    assert_close(layers[1].weights.grad, O.softmax_backward(tabs[1][2], O.dense_backward_w(h1, tabs[1][0][0], tabs[1][0][1],
+                                                                                           tabs[1][1], gy2)), 2e-3, "fp16 g2")

@@ -21,7 +21,7 @@ pytestmark = pytest.mark.gpu
 
 def _with_workspace(x, a, b, g, gy, dtype):
     out, K = a.shape
-    ws = torch.empty(int(L.lib().clb_difflogic_workspace_bytes(out, K, x.shape[1], L.dtype_code(dtype))),
+    ws = torch.empty(int(L.lib().clb_difflogic_workspace_bytes(x.shape[0], out, K, x.shape[1], L.dtype_code(dtype))),
                      dtype=torch.uint8, device="cuda")
     gw = torch.empty(out, K, dtype=dtype, device="cuda")
     st = L.lib().clb_difflogic_backward_w(L.dtype_code(dtype), x.data_ptr(), x.shape[0], x.shape[1], a.data_ptr(),
