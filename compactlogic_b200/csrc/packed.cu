@@ -13,6 +13,8 @@
 // tests), and the final layer can be fused with it so its outputs are never stored.
 #include <cuda_runtime.h>
 
+#include <stdlib.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -193,8 +195,8 @@ __device__ __forceinline__ uint64_t word_or_zero(const uint64_t* __restrict__ x,
 // One packed layer.  Each lane owns V consecutive word columns (V = 2: one 16-byte load per operand),
 // TW lanes span TW*V columns, 32/TW neurons share a warp row, and each thread handles R neurons
 // spaced 32/TW apart so that 2R independent loads are in flight per thread.
-template <int R, int V>
-__global__ void __launch_bounds__(256)
+template <int R, int V, int MINB = 1>
+__global__ void __launch_bounds__(256, MINB)
 packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
                     const uint8_t* __restrict__ sel_gate, int64_t n_out, uint64_t* __restrict__ y, int64_t ldy,
                     int tw_log2) {
@@ -476,9 +478,27 @@ cudaError_t launch_packed_select(const int32_t* slots, const uint8_t* gates, con
     return cudaGetLastError();
 }
 
+// Tuning overrides (read once): CLB_PACKED_R neurons per thread (2/4/8), CLB_PACKED_MINB 4 = cap registers
+// for 4 resident CTAs per SM.
+int packed_env(const char* name, int dflt) {
+    const char* v = getenv(name);
+    return v != nullptr ? atoi(v) : dflt;
+}
+
+template <int R, int V>
+void packed_layer_go(dim3 grid, cudaStream_t s, int minb, const uint64_t* x, int64_t ldx, int64_t nwords, const int2* ab,
+                     const uint8_t* g, int64_t n_out, uint64_t* y, int64_t ldy, int tw_log2) {
+    if (minb == 4)
+        packed_layer_kernel<R, V, 4><<<grid, 256, 0, s>>>(x, ldx, nwords, ab, g, n_out, y, ldy, tw_log2);
+    else
+        packed_layer_kernel<R, V, 1><<<grid, 256, 0, s>>>(x, ldx, nwords, ab, g, n_out, y, ldy, tw_log2);
+}
+
 cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
                                 const uint8_t* sel_gate, int64_t n_out, uint64_t* y, int64_t ldy, cudaStream_t s) {
     if (n_out == 0 || nwords == 0) return cudaSuccess;
+    static const int R = packed_env("CLB_PACKED_R", 4);
+    static const int minb = packed_env("CLB_PACKED_MINB", 1);
     const bool v2 = nwords % 2 == 0 && ldx % 2 == 0 && ldy % 2 == 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0;
     const int V = v2 ? 2 : 1;
     const int64_t cols = nwords / V;  // lane-owned column groups
@@ -486,16 +506,18 @@ cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, 
     while ((1 << tw_log2) < cols && tw_log2 < 5) ++tw_log2;
     const int64_t TW = 1 << tw_log2;
     const int64_t npw = 32 / TW;
-    constexpr int R = 4;
-    const int64_t warps_needed = ceil_div64(n_out, npw * R);
+    const int r = (R == 2 || R == 8) ? R : 4;
+    const int64_t warps_needed = ceil_div64(n_out, npw * r);
     const int64_t by = std::min<int64_t>(ceil_div64(warps_needed, 8), 65535);
     dim3 grid((unsigned)ceil_div64(cols, TW), (unsigned)by);
-    if (v2)
-        packed_layer_kernel<R, 2><<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate,
-                                                       n_out, y, ldy, tw_log2);
-    else
-        packed_layer_kernel<R, 1><<<grid, 256, 0, s>>>(x, ldx, nwords, reinterpret_cast<const int2*>(sel_ab), sel_gate,
-                                                       n_out, y, ldy, tw_log2);
+    const int2* ab = reinterpret_cast<const int2*>(sel_ab);
+    if (v2) {
+        if (r == 2) packed_layer_go<2, 2>(grid, s, minb, x, ldx, nwords, ab, sel_gate, n_out, y, ldy, tw_log2);
+        else if (r == 8) packed_layer_go<8, 2>(grid, s, minb, x, ldx, nwords, ab, sel_gate, n_out, y, ldy, tw_log2);
+        else packed_layer_go<4, 2>(grid, s, minb, x, ldx, nwords, ab, sel_gate, n_out, y, ldy, tw_log2);
+    } else {
+        packed_layer_go<4, 1>(grid, s, 1, x, ldx, nwords, ab, sel_gate, n_out, y, ldy, tw_log2);
+    }
     return cudaGetLastError();
 }
 
