@@ -478,8 +478,8 @@ cudaError_t launch_packed_select(const int32_t* slots, const uint8_t* gates, con
     return cudaGetLastError();
 }
 
-// Tuning overrides (read once): CLB_PACKED_R neurons per thread (2/4/8), CLB_PACKED_MINB 4 = cap registers
-// for 4 resident CTAs per SM.
+// Tuning overrides (read once): CLB_PACKED_R neurons per thread (2/4/8), CLB_PACKED_MINB registers capped for 4
+// (default) or 1 resident CTAs per SM (measured: 437 vs 459-558 ms per c4 pass at 128-word chunks).
 int packed_env(const char* name, int dflt) {
     const char* v = getenv(name);
     return v != nullptr ? atoi(v) : dflt;
@@ -498,7 +498,7 @@ cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, 
                                 const uint8_t* sel_gate, int64_t n_out, uint64_t* y, int64_t ldy, cudaStream_t s) {
     if (n_out == 0 || nwords == 0) return cudaSuccess;
     static const int R = packed_env("CLB_PACKED_R", 4);
-    static const int minb = packed_env("CLB_PACKED_MINB", 1);
+    static const int minb = packed_env("CLB_PACKED_MINB", 4);
     const bool v2 = nwords % 2 == 0 && ldx % 2 == 0 && ldy % 2 == 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0;
     const int V = v2 ? 2 : 1;
     const int64_t cols = nwords / V;  // lane-owned column groups
