@@ -10,6 +10,7 @@ Samples are processed in chunks of ``chunk_words`` words (64 samples each): all 
 run back to back so the chunk's intermediate activations (n_out x chunk_words x 8 bytes per layer)
 stay in the 126 MB L2 instead of round-tripping through HBM.
 """
+import math
 from typing import List, Optional
 
 import torch
@@ -77,8 +78,8 @@ class PackedLogicNet:
     # ------------------------------------------------------------------
     def pack(self, x: torch.Tensor) -> torch.Tensor:
         """[batch, features] (or [batch, C, H, W]) {0,1} -> [features, ceil(batch/64)] uint64."""
-        x = x.reshape(x.shape[0], -1)
-        if x.dtype not in (torch.float32, torch.float64, torch.bfloat16):
+        x = x.reshape(x.shape[0], math.prod(x.shape[1:]))
+        if x.dtype not in (torch.float32, torch.float64, torch.bfloat16, torch.float16):
             x = x.to(torch.float32)
         if x.stride(1) != 1:
             x = x.contiguous()
@@ -94,8 +95,8 @@ class PackedLogicNet:
     def pack_raw(self, x: torch.Tensor, nthr: int) -> torch.Tensor:
         """Raw inputs [batch, C, H, W] (or [batch, F]) in [0, 1] -> [nthr*F, W] packed words, thresholding at
         (i+1)/(nthr+1) in the reference's order (experiments/experiment_script.py:92) in the same pass."""
-        x = x.reshape(x.shape[0], -1)
-        if x.dtype not in (torch.float32, torch.float64, torch.bfloat16):
+        x = x.reshape(x.shape[0], math.prod(x.shape[1:]))
+        if x.dtype not in (torch.float32, torch.float64, torch.bfloat16, torch.float16):
             x = x.to(torch.float32)
         if x.stride(1) != 1:
             x = x.contiguous()
@@ -163,6 +164,8 @@ class PackedLogicNet:
             raise ValueError("xw must be [in_features, words] with unit column stride")
         if counts is None:
             counts = torch.empty(batch, self.k, dtype=torch.int32, device=self.device)
+        if batch == 0 or xw.shape[1] == 0:
+            return counts.zero_()
         if not (self.use_graphs if use_graph is None else use_graph):
             self._run(xw, batch, counts)
             return counts

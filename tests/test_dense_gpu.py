@@ -309,3 +309,32 @@ def test_fp16_reference_api_and_layers():
     gy2 = O.group_sum_backward(np.ones_like(lg), 100, 5, 2.0).T
     assert_close(layers[1].weights.grad, O.softmax_backward(tabs[1][2], O.dense_backward_w(h1, tabs[1][0][0], tabs[1][0][1],
                                                                                            tabs[1][1], gy2)), 2e-3, "fp16 g2")
+
+
+@pytest.mark.parametrize("K", [128, 33])
+def test_many_candidate_gates(K):
+    """K beyond the specialised 4/8/16 paths (the reference's LogicLayer docstring default is 128)."""
+    x, a, b, logits, g, gy = rand_dense(K, 90, 70, K, 40)
+    spec = _spec(a, b, g, 90)
+    xt = cuda(x, torch.float32).requires_grad_(True)
+    w = cuda(logits, torch.float32).requires_grad_(True)
+    y = LogicLayerFn.apply(xt, w, spec)
+    p = O.softmax(logits)
+    assert_close(y, O.dense_forward(x, a, b, p, g), 1e-5, "y")
+    y.backward(cuda(gy, torch.float32))
+    assert_close(xt.grad, O.dense_backward_x(x, a, b, p, g, gy), 1e-5, "gx")
+    assert_close(w.grad, O.softmax_backward(p, O.dense_backward_w(x, a, b, g, gy)), 1e-5, "gw")
+
+
+def test_empty_batch():
+    torch.manual_seed(0)
+    model = cl.fuse_groupsum(torch.nn.Sequential(cl.LogicLayer(20, 30, num_gates=4), cl.LogicLayer(30, 24, num_gates=4),
+                                                 cl.GroupSum(4, 1.0))).cuda()
+    x = torch.zeros(0, 20, device="cuda", requires_grad=True)
+    out = model(x)
+    assert out.shape == (0, 4)
+    out.sum().backward()
+    assert torch.count_nonzero(model[0].weights.grad) == 0
+    model.eval()
+    assert model(torch.zeros(0, 20, device="cuda")).shape == (0, 4)
+    assert cl.PackedLogicNet(model)(torch.zeros(0, 20, device="cuda")).shape == (0, 4)
