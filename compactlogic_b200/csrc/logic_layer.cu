@@ -200,8 +200,8 @@ __device__ __forceinline__ void gather(const T* __restrict__ x, int idx, int64_t
 // With GroupSum fused (compactlogic.py:460-465), y is never written; per-class column sums are
 // accumulated into gs.acc instead.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC, int MINB = 1, int UNR = 4>
-__global__ void __launch_bounds__(kThreads, MINB)
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kThreads)
 logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, const GroupSumArgs gs,
                      const bool use_gs, const int TN) {
     using A = typename Acc<T>::type;
@@ -233,7 +233,7 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
             const int ns = st.ns[t];
             const int2* ab = st.ab + t * K;
             const A4<A>* cf = st.cf + t * K;
-#pragma unroll UNR
+#pragma unroll 4
             for (int s = 0; s < ns; ++s) {
                 const int2 pr = ab[s];
                 const A4<A> c = cf[s];
@@ -300,8 +300,8 @@ constexpr int log2c(int n) { return n <= 1 ? 0 : 1 + log2c(n / 2); }
 // ([nchunks, n_out, K], deterministic) and folded by the finalize kernel.
 // KT > 0: K is a compile-time constant and the K partial sums live in registers.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC, int KT, int MINB = 1>
-__global__ void __launch_bounds__(kThreads, MINB)
+template <typename T, int VEC, int KT>
+__global__ void __launch_bounds__(kThreads)
 logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict__ gy, const int64_t ldgy,
                       const GroupSumArgs gs, const bool use_gs, typename Acc<T>::type* __restrict__ gx,
                       const int64_t ldgx, typename Acc<T>::type* __restrict__ part, const int TN) {
@@ -745,23 +745,10 @@ int env_int(const char* name, int dflt) {
     return v != nullptr ? atoi(v) : dflt;
 }
 
-// Tuning overrides (read once): CLB_TN neurons per CTA (32/64/128), CLB_FWD_MINB / CLB_BWD_MINB minimum
-// resident CTAs per SM (register cap), CLB_FWD_UNROLL slot-loop unroll of the forward (4/8).
+// Tuning override (read once): CLB_TN neurons per CTA (32 / 64 / 128; default 64).
 int tn_max() {
     static const int v = env_int("CLB_TN", 64);
     return (v == 32 || v == 128) ? v : 64;
-}
-int fwd_minb() {
-    static const int v = env_int("CLB_FWD_MINB", 1);
-    return v == 6 ? 6 : 1;
-}
-int fwd_unroll() {
-    static const int v = env_int("CLB_FWD_UNROLL", 4);
-    return v == 8 ? 8 : 4;
-}
-int bwd_minb() {
-    static const int v = env_int("CLB_BWD_MINB", 1);
-    return v == 5 ? 5 : 1;
 }
 
 // Column-chunk width: LPN lanes per neuron (32 = one neuron per warp step, 32*VEC columns per chunk).
@@ -920,9 +907,6 @@ cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* 
         k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
     } else if (vec) {
         auto k = logic_forward_kernel<T, vmax<T>()>;
-        if (fwd_minb() == 6 && fwd_unroll() == 8) k = logic_forward_kernel<T, vmax<T>(), 6, 8>;
-        else if (fwd_minb() == 6) k = logic_forward_kernel<T, vmax<T>(), 6, 4>;
-        else if (fwd_unroll() == 8) k = logic_forward_kernel<T, vmax<T>(), 1, 8>;
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
     } else {
@@ -938,7 +922,6 @@ cudaError_t bwd_launch(const LayerArgs& a, const void* gy, int64_t ldgy, const G
                        void* gx, int64_t ldgx, void* part, dim3 grid, size_t smem, int TN, cudaStream_t s) {
     using A = typename Acc<T>::type;
     auto k = logic_backward_kernel<T, VEC, KT>;
-    if (bwd_minb() == 5 && VEC == vmax<T>()) k = logic_backward_kernel<T, VEC, KT, 5>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<const A*>(gy), ldgy, g, use_gs, reinterpret_cast<A*>(gx), ldgx,
                                    reinterpret_cast<A*>(part), TN);
