@@ -152,24 +152,43 @@ def c2_bytes_per_step(B):
     return fwd + bwd
 
 
+def clip_sharded(params, max_norm):
+    """clip_grad_norm_ over parameters sharded across the ranks (one all-reduce of the squared norm)."""
+    sq = torch.stack([p.grad.float().pow(2).sum() for p in params if p.grad is not None]).sum()
+    if dist.is_initialized():
+        dist.all_reduce(sq)
+    coef = torch.clamp(max_norm / (sq.sqrt() + 1e-6), max=1.0)
+    for p in params:
+        if p.grad is not None:
+            p.grad.mul_(coef)
+
+
 def bench_c2(args, dev, rank, world):
     from compactlogic_b200 import _lib
     from compactlogic_b200.functional import TIMER
     from compactlogic_b200.parallel import GradAllReduce
+    width = args.parallel == "width"
     model = build_c2(dev)
+    if width:
+        # neuron-parallel: every rank runs the whole batch on its share of each layer's neurons
+        from compactlogic_b200.sharded import shard_width
+        model = shard_width(model)
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.Adam(params, lr=0.01, fused=True)
-    sync = GradAllReduce(params)
+    sync = None if width else GradAllReduce(params)
     B = C2["batch"]
-    x_host, y_host = c2_inputs(1000 + rank, B)
+    x_host, y_host = c2_inputs(1000 + (0 if width else rank), B)
     x_dev, y_dev = x_host.to(dev), y_host.to(dev)
 
     def step(x, y):
         opt.zero_grad(set_to_none=True)
         loss = torch.nn.functional.cross_entropy(model(x), y)
         loss.backward()
-        sync.finish()
-        torch.nn.utils.clip_grad_norm_(params, 10.0)
+        if sync is not None:
+            sync.finish()
+            torch.nn.utils.clip_grad_norm_(params, 10.0)
+        else:
+            clip_sharded(params, 10.0)
         opt.step()
         return loss
 
@@ -210,20 +229,25 @@ def bench_c2(args, dev, rank, world):
                 "algorithmic_bytes_per_launch": round(tot_b / n), "launches": n, "avg_ms": round(tot_ms / n, 4),
                 "shares": {k: round(v[1] / sum(w[1] for w in kern.values()), 3) for k, v in kern.items()}}
     step_bytes = c2_bytes_per_step(B)
+    gb = B if width else B * world
     res = {
-        "metric": "train_samples_per_s", "value": round(world * B / (ms / 1e3), 1), "unit": "samples/s",
+        "metric": "train_samples_per_s", "value": round(gb / (ms / 1e3), 1), "unit": "samples/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if width else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
         "config": {"workload": f"c2: 784 -> {C2['layers']}x LogicLayer(64000, K=16) -> GroupSum(10, tau=10); CE, "
-                               "all-reduce, clip 10, Adam", "batch_per_gpu": B, "global_batch": B * world,
-                   "parallelism": f"dp{world}", "l2": "per-layer activations 262 MB > L2 126 MB (no flush)"},
+                               + ("width-sharded neurons, peer-fused gather / reduce-scatter" if width else
+                                  "all-reduce") + ", clip 10, Adam",
+                   "batch_per_gpu": B, "global_batch": gb,
+                   "parallelism": f"width{world}" if width else f"dp{world}",
+                   "l2": "per-layer activations 262 MB > L2 126 MB (no flush)"},
         "step_hbm_bytes_algorithmic": step_bytes,
         "step_hbm_frac": round(step_bytes / (ms / 1e3) / 1e9 / hbm, 4),
         "roofline": roof,
         "kernels": {k: {"launches": v[0], "ms_total": round(v[1], 3), "gb": round(v[2] / 1e9, 3)}
                     for k, v in kern.items()},
         "clocks": clk.summary(),
-        "e2e": {"value": round(world * B / (ms_e2e / 1e3), 1), "unit": "samples/s",
+        "e2e": {"value": round(gb / (ms_e2e / 1e3), 1), "unit": "samples/s",
                 "h2d_bytes_per_step": x_host.numel() * 4 + y_host.numel() * 8, "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches),
     }
@@ -513,6 +537,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-refcuda", action="store_true", help="skip the reference-CUDA-kernel step timing")
     ap.add_argument("--chunk-words", type=int, default=128)
+    ap.add_argument("--parallel", default="dp", choices=["dp", "width"],
+                    help="c2 multi-GPU scheme: data parallel (default) or width-sharded neurons")
     ap.add_argument("--layers", type=int, default=None, help="override the c2 depth (profiling on a smaller case)")
     ap.add_argument("--samples", type=int, default=None, help="override the c4 sample count (profiling)")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU work per baseline sample")

@@ -53,6 +53,15 @@ _SIGS = {
     "clb_logic_backward": (_int, [_int, _p, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _int, _p, _i64, _p, _i64,
                                   _i64, _i64, _dbl, _p, _i64, _int, _i64, _p, _i64, _p]),
     "clb_logic_grad_finalize": (_int, [_int, _p, _i64, _i64, _i64, _i64, _int, _p, _p, _p]),
+    "clb_logic_forward_peers": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _i64, _int, _p, _p, _int, _p, _int, _i64,
+                                       _p]),
+    "clb_logic_backward_peers": (_int, [_int, _p, _i64, _i64, _p, _i64, _i64, _int, _p, _p, _int, _p, _int, _i64, _p,
+                                        _i64, _int, _i64, _p, _i64, _p]),
+    "clb_peer_alloc": (_int, [_sz, ctypes.POINTER(_p)]),
+    "clb_peer_free": (_int, [_p]),
+    "clb_ipc_export": (_int, [_p, _p]),
+    "clb_ipc_import": (_int, [_p, ctypes.POINTER(_p)]),
+    "clb_ipc_close": (_int, [_p]),
     "clb_transpose": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "clb_cast": (_int, [_int, _p, _int, _p, _i64, _p]),
     "clb_pack_inputs": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _p]),

@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <cmath>
 #include <string>
 
@@ -214,6 +215,105 @@ int clb_logic_grad_finalize(int dtype, const void* partials, int64_t nchunks, in
     const LayerArgs a = layer(dtype, nullptr, 0, 0, nullptr, n_out, K, group, weight_mode, weights, nullptr, nullptr, false);
     return cuda_status(launch_grad_finalize(a, partials, nchunks, grad_w, dtype, S(stream)), "grad_finalize");
 }
+
+// ----------------------------------------------------------------------------------------------
+// width-sharded training: peer-stored forward, peer-summed backward, IPC-registered buffers
+// ----------------------------------------------------------------------------------------------
+namespace {
+int set_peers(PeerArgs& a, const void* const* peers, int n_peers, const char* what) {
+    if (n_peers < 1 || n_peers > kMaxPeers || !peers)
+        return fail(CLB_ERR_INVALID, "%s: n_peers %d outside 1..%d", what, n_peers, kMaxPeers);
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(peers[0]) & 15;
+    for (int p = 0; p < n_peers; ++p) {
+        if (!peers[p]) return fail(CLB_ERR_INVALID, "%s: null peer pointer %d", what, p);
+        // every rank's buffer is addressed with one stride and one vector width
+        if ((reinterpret_cast<uintptr_t>(peers[p]) & 15) != mis)
+            return fail(CLB_ERR_INVALID, "%s: peer pointers differ in 16-byte alignment", what);
+        a.p[p] = const_cast<void*>(peers[p]);
+    }
+    a.n = n_peers;
+    return CLB_OK;
+}
+}  // namespace
+
+int clb_logic_forward_peers(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
+                            const int32_t* slots, int64_t n_out, int64_t K, int weight_mode, const void* weights,
+                            const uint8_t* gates, int has_pad, void* const* y_peers, int n_peers, int64_t ldy,
+                            clb_stream_t stream) {
+    int st = check_layer(dtype, n_out, K, 1, weight_mode, weights, gates, nullptr, slots);
+    if (st) return st;
+    if (weight_mode == CLB_W_SELECT) return fail(CLB_ERR_INVALID, "forward_peers: select mode not supported");
+    if (ncols < 0 || ldx < ncols || ldy < ncols) return fail(CLB_ERR_INVALID, "forward_peers: ld < ncols");
+    const LayerArgs a = layer(dtype, x, ldx, ncols, slots, n_out, K, 1, weight_mode, weights, gates, nullptr, has_pad,
+                              in_features);
+    PeerArgs pa{};
+    if ((st = set_peers(pa, const_cast<const void* const*>(y_peers), n_peers, "forward_peers"))) return st;
+    if (ncols == 0 || n_out == 0) return CLB_OK;
+    if (!x) return fail(CLB_ERR_INVALID, "forward_peers: null x");
+    return cuda_status(launch_logic_forward(a, y_peers[0], ldy, nullptr, S(stream), &pa), "logic_forward_peers");
+}
+
+int clb_logic_backward_peers(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots,
+                             int64_t n_out, int64_t K, int weight_mode, const void* weights, const uint8_t* gates,
+                             int has_pad, const void* const* gy_peers, int n_peers, int64_t ldgy, void* grad_x,
+                             int64_t ldgx, int zero_grad_x, int64_t in_features, void* partials,
+                             int64_t partials_chunks, clb_stream_t stream) {
+    int st = check_layer(dtype, n_out, K, 1, weight_mode, weights, gates, nullptr, slots,
+                         grad_x != nullptr || weight_mode == CLB_W_LOGITS);
+    if (st) return st;
+    if (weight_mode == CLB_W_SELECT) return fail(CLB_ERR_INVALID, "backward_peers: select mode has no gradient");
+    if (ncols < 0 || ldx < ncols || ldgy < ncols) return fail(CLB_ERR_INVALID, "backward_peers: ld < ncols");
+    if (grad_x && (ldgx < ncols || in_features < 0)) return fail(CLB_ERR_INVALID, "backward_peers: ldgx < ncols");
+    const LayerArgs a = layer(dtype, x, ldx, ncols, slots, n_out, K, 1, weight_mode, weights, gates, nullptr, has_pad,
+                              in_features);
+    PeerArgs pa{};
+    if ((st = set_peers(pa, gy_peers, n_peers, "backward_peers"))) return st;
+    if (grad_x && zero_grad_x) {
+        cudaError_t e = cudaMemsetAsync(grad_x, 0, acc_size(dtype) * (size_t)in_features * (size_t)ldgx, S(stream));
+        if (e != cudaSuccess) return cuda_status(e, "backward_peers: memset grad_x", 0);
+    }
+    if (ncols == 0 || n_out == 0) return CLB_OK;
+    if (!x) return fail(CLB_ERR_INVALID, "backward_peers: null x");
+    if (partials) {
+        const int64_t need = clb_logic_backward_chunks(dtype, x, ldx, ncols, in_features, gy_peers[0], ldgy, nullptr, 0,
+                                                       grad_x, ldgx);
+        if (need != partials_chunks)
+            return fail(CLB_ERR_INVALID, "backward_peers: partials sized for %lld chunks, this call needs %lld",
+                        (long long)partials_chunks, (long long)need);
+    }
+    return cuda_status(launch_logic_backward(a, gy_peers[0], ldgy, nullptr, grad_x, ldgx, partials, partials_chunks,
+                                             S(stream), &pa),
+                       "logic_backward_peers");
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == CLB_IPC_HANDLE_BYTES, "IPC handle size");
+
+int clb_peer_alloc(size_t bytes, void** ptr) {
+    if (!ptr) return fail(CLB_ERR_INVALID, "peer_alloc: null ptr");
+    *ptr = nullptr;
+    return cuda_status(cudaMalloc(ptr, bytes ? bytes : 256), "peer_alloc", 0);
+}
+
+int clb_peer_free(void* ptr) { return ptr ? cuda_status(cudaFree(ptr), "peer_free", 0) : CLB_OK; }
+
+int clb_ipc_export(const void* ptr, void* handle) {
+    if (!ptr || !handle) return fail(CLB_ERR_INVALID, "ipc_export: null pointer");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) return cuda_status(e, "ipc_export", 0);
+    memcpy(handle, &h, sizeof(h));
+    return CLB_OK;
+}
+
+int clb_ipc_import(const void* handle, void** ptr) {
+    if (!ptr || !handle) return fail(CLB_ERR_INVALID, "ipc_import: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *ptr = nullptr;
+    return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "ipc_import", 0);
+}
+
+int clb_ipc_close(void* ptr) { return ptr ? cuda_status(cudaIpcCloseMemHandle(ptr), "ipc_close", 0) : CLB_OK; }
 
 int clb_transpose(int elem_bytes, const void* src, int64_t rows, int64_t cols, int64_t ld_src, void* dst,
                   int64_t ld_dst, clb_stream_t stream) {

@@ -7,6 +7,8 @@
 
 namespace clb {
 
+constexpr int kMaxPeers = 8;
+
 // Arguments of one soft / select logic-layer pass over feature-major activations.
 //   x      [in_features, ldx] element type `dtype`; columns [0, ncols) are processed.
 //   slots  [n_out, K] pairs (a, b) of input feature ids; -1 reads as the constant 0 (padding).
@@ -29,6 +31,16 @@ struct LayerArgs {
     int64_t in_features;   // rows of x (0 = unknown); selects the column-chunk geometry
 };
 
+// Width-sharded training (each rank owns a contiguous share of the neurons): the number of ranks and
+// one pointer per rank.  Forward stores row j of y to p[r] + j*ldy for every rank r (the activation
+// all-gather, fused into the epilogue as NVLink stores); backward reads grad_y[j] as the sum over r of
+// p[r][j*ldgy] (the gradient reduce-scatter, fused into the grad_y load as NVLink reads).  Passed as
+// its own kernel argument: growing LayerArgs changes the register allocation of the single-GPU kernels.
+struct PeerArgs {
+    int n;
+    void* p[kMaxPeers];
+};
+
 struct GroupSumArgs {
     void* acc;         // [k, ld] arithmetic type: forward accumulates sum_j y[j, col] per class
     const void* grad;  // [k, ld] arithmetic type: backward reads d loss / d class sum
@@ -39,14 +51,15 @@ struct GroupSumArgs {
 };
 
 cudaError_t launch_logic_forward(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs,
-                                 cudaStream_t s);
+                                 cudaStream_t s, const PeerArgs* peers = nullptr);
 
 // Fused backward: reads x once per slot and produces both the per-chunk partial sums of
 // d loss / d prob (when `partials` != null) and the scattered activation gradient (when gx != null,
 // accumulated into a pre-zeroed buffer).
 // `part_chunks` must equal logic_backward_chunks(...) for the same arguments (checked).
 cudaError_t launch_logic_backward(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs* gs,
-                                  void* gx, int64_t ldgx, void* partials, int64_t part_chunks, cudaStream_t s);
+                                  void* gx, int64_t ldgx, void* partials, int64_t part_chunks, cudaStream_t s,
+                                  const PeerArgs* peers = nullptr);
 int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void* x, int64_t ldgy,
                               const void* gy, int64_t ld_gs, const void* gs_grad, int64_t ldgx, const void* gx,
                               int64_t in_features);

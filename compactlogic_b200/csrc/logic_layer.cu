@@ -200,10 +200,10 @@ __device__ __forceinline__ void gather(const T* __restrict__ x, int idx, int64_t
 // With GroupSum fused (compactlogic.py:460-465), y is never written; per-class column sums are
 // accumulated into gs.acc instead.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC>
+template <typename T, int VEC, bool PEERS>
 __global__ void __launch_bounds__(kThreads)
 logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, const GroupSumArgs gs,
-                     const bool use_gs, const int TN) {
+                     const bool use_gs, const int TN, const PeerArgs pa) {
     using A = typename Acc<T>::type;
     extern __shared__ __align__(16) unsigned char smem[];
     const int K = a.K;
@@ -249,7 +249,14 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
             }
         }
         if (!use_gs) {
-            if (active) store_from_acc<T, VEC>(y + j * ldy + col, acc);
+            if (active) {
+                if (!PEERS) {
+                    store_from_acc<T, VEC>(y + j * ldy + col, acc);
+                } else {
+                    for (int p = 0; p < pa.n; ++p)
+                        store_from_acc<T, VEC>(reinterpret_cast<T*>(pa.p[p]) + j * ldy + col, acc);
+                }
+            }
         } else {
             const int64_t cls = j / gs.size;
             if (cls != gcls) {
@@ -263,6 +270,7 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
         }
     }
     if (use_gs && gcls >= 0 && active) red_add<VEC>(reinterpret_cast<A*>(gs.acc) + gcls * gs.ld + col, gacc);
+    if (PEERS) __threadfence_system();  // peer stores complete before the host-side barrier that follows
 }
 
 // Butterfly reduce-scatter of N per-lane values over the warp: afterwards lane l holds the warp sum
@@ -300,11 +308,11 @@ constexpr int log2c(int n) { return n <= 1 ? 0 : 1 + log2c(n / 2); }
 // ([nchunks, n_out, K], deterministic) and folded by the finalize kernel.
 // KT > 0: K is a compile-time constant and the K partial sums live in registers.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC, int KT>
+template <typename T, int VEC, int KT, bool PEERS>
 __global__ void __launch_bounds__(kThreads)
 logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict__ gy, const int64_t ldgy,
                       const GroupSumArgs gs, const bool use_gs, typename Acc<T>::type* __restrict__ gx,
-                      const int64_t ldgx, typename Acc<T>::type* __restrict__ part, const int TN) {
+                      const int64_t ldgx, typename Acc<T>::type* __restrict__ part, const int TN, const PeerArgs pa) {
     using A = typename Acc<T>::type;
     extern __shared__ __align__(16) unsigned char smem[];
     const int K = KT > 0 ? KT : a.K;
@@ -329,8 +337,16 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
                 load_acc<A, VEC>(gsg + (j / gs.size) * gs.ld + col, g);
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) g[i] *= (A)gs.scale;
-            } else {
+            } else if (!PEERS) {
                 load_acc<A, VEC>(gy + j * ldgy + col, g);
+            } else {
+                load_acc<A, VEC>(reinterpret_cast<const A*>(pa.p[0]) + j * ldgy + col, g);
+                for (int p = 1; p < pa.n; ++p) {
+                    A h[VEC];
+                    load_acc<A, VEC>(reinterpret_cast<const A*>(pa.p[p]) + j * ldgy + col, h);
+#pragma unroll
+                    for (int i = 0; i < VEC; ++i) g[i] += h[i];
+                }
             }
         } else {
 #pragma unroll
@@ -872,14 +888,24 @@ cudaError_t bwd_narrow(const LayerArgs& a, const void* gy, int64_t ldgy, const G
 }
 
 template <typename T>
-int bwd_lpn(const LayerArgs& a, bool vec, int V, const void* gx) {
+int bwd_lpn(const LayerArgs& a, bool vec, int V, const void* gx, bool peers) {
     using A = typename Acc<T>::type;
-    if (!vec || V != vmax<T>() || std::is_same<T, double>::value) return 32;
+    if (!vec || V != vmax<T>() || std::is_same<T, double>::value || peers) return 32;
     return pick_lpn(a.in_features, V, sizeof(T) + (gx != nullptr ? sizeof(A) : 0), true);
 }
 
+template <typename T, int VEC>
+void fwd_launch(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs& g, bool use_gs, dim3 grid, size_t smem,
+                int TN, cudaStream_t s, const PeerArgs& pa) {
+    // the peer-store epilogue is a separate instantiation so the single-GPU kernel keeps its registers
+    auto k = pa.n ? logic_forward_kernel<T, VEC, true> : logic_forward_kernel<T, VEC, false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, use_gs, TN, pa);
+}
+
 template <typename T>
-cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s) {
+cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s,
+                  const PeerArgs& pa) {
     using A = typename Acc<T>::type;
     const int K = a.K;
     const int TN = choose_tn(stage_bytes<A>(1, K, false));
@@ -894,48 +920,41 @@ cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* 
     const int V = vec ? (half ? 2 : wide ? 8 : vmax<T>()) : 1;
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-    const int lpn = (vec && !wide && !half && !std::is_same<T, double>::value) ? pick_lpn(a.in_features, V, sizeof(T), false)
+    const int lpn = (vec && !wide && !half && !std::is_same<T, double>::value && pa.n == 0) ? pick_lpn(a.in_features, V, sizeof(T), false)
                                                                                   : 32;
     if (lpn < 32) return fwd_narrow<T>(a, y, ldy, gs, lpn, s);
     if (wide) {
-        auto k = logic_forward_kernel<T, 8>;
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
+        fwd_launch<T, 8>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
     } else if (half) {
-        auto k = logic_forward_kernel<T, 2>;
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
+        fwd_launch<T, 2>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
     } else if (vec) {
-        auto k = logic_forward_kernel<T, vmax<T>()>;
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
+        fwd_launch<T, vmax<T>()>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
     } else {
-        auto k = logic_forward_kernel<T, 1>;
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, gs != nullptr, TN);
+        fwd_launch<T, 1>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
     }
     return cudaGetLastError();
 }
 
 template <typename T, int VEC, int KT>
 cudaError_t bwd_launch(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs& g, bool use_gs,
-                       void* gx, int64_t ldgx, void* part, dim3 grid, size_t smem, int TN, cudaStream_t s) {
+                       void* gx, int64_t ldgx, void* part, dim3 grid, size_t smem, int TN, cudaStream_t s,
+                       const PeerArgs& pa) {
     using A = typename Acc<T>::type;
-    auto k = logic_backward_kernel<T, VEC, KT>;
+    auto k = pa.n ? logic_backward_kernel<T, VEC, KT, true> : logic_backward_kernel<T, VEC, KT, false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<const A*>(gy), ldgy, g, use_gs, reinterpret_cast<A*>(gx), ldgx,
-                                   reinterpret_cast<A*>(part), TN);
+                                   reinterpret_cast<A*>(part), TN, pa);
     return cudaGetLastError();
 }
 
 template <typename T, int VEC>
 cudaError_t bwd_k(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs& g, bool use_gs, void* gx,
-                  int64_t ldgx, void* part, dim3 grid, size_t smem, int TN, cudaStream_t s) {
+                  int64_t ldgx, void* part, dim3 grid, size_t smem, int TN, cudaStream_t s, const PeerArgs& pa) {
     switch (a.K) {
-        case 4: return bwd_launch<T, VEC, 4>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s);
-        case 8: return bwd_launch<T, VEC, 8>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s);
-        case 16: return bwd_launch<T, VEC, 16>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s);
-        default: return bwd_launch<T, VEC, 0>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s);
+        case 4: return bwd_launch<T, VEC, 4>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s, pa);
+        case 8: return bwd_launch<T, VEC, 8>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s, pa);
+        case 16: return bwd_launch<T, VEC, 16>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s, pa);
+        default: return bwd_launch<T, VEC, 0>(a, gy, ldgy, g, use_gs, gx, ldgx, part, grid, smem, TN, s, pa);
     }
 }
 
@@ -957,7 +976,7 @@ inline bool bwd_wide_ok(const LayerArgs& a, int64_t ldgy, const GroupSumArgs* gs
 
 template <typename T>
 cudaError_t bwd_t(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs* gs, void* gx, int64_t ldgx,
-                  void* part, int64_t part_chunks, cudaStream_t s) {
+                  void* part, int64_t part_chunks, cudaStream_t s, const PeerArgs& pa) {
     using A = typename Acc<T>::type;
     const int K = a.K;
     const int TN = choose_tn(stage_bytes<A>(1, K, true));
@@ -969,7 +988,7 @@ cudaError_t bwd_t(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupS
     const bool wide = vec && bv == 8 && bwd_wide_ok(a, ldgy, gs, ldgx);
     const bool half = vec && bv == 2;
     const int V = vec ? (half ? 2 : wide ? 8 : vmax<T>()) : 1;
-    const int lpn = bwd_lpn<T>(a, vec, V, gx);
+    const int lpn = bwd_lpn<T>(a, vec, V, gx, pa.n != 0);
     if (lpn < 32) {
         if (part != nullptr && ceil_div64(a.ncols, lpn * V) != part_chunks) return cudaErrorInvalidValue;
         return bwd_narrow<T>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, lpn, s);
@@ -977,10 +996,10 @@ cudaError_t bwd_t(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupS
     dim3 grid((unsigned)ceil_div64(a.n_out, TN), (unsigned)ceil_div64(a.ncols, 32 * V));
     if (part != nullptr && (int64_t)grid.y != part_chunks) return cudaErrorInvalidValue;  // scratch sized for another split
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-    if (half) return bwd_k<T, 2>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
-    if (wide) return bwd_k<T, 8>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
-    if (vec) return bwd_k<T, vmax<T>()>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
-    return bwd_k<T, 1>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s);
+    if (half) return bwd_k<T, 2>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s, pa);
+    if (wide) return bwd_k<T, 8>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s, pa);
+    if (vec) return bwd_k<T, vmax<T>()>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s, pa);
+    return bwd_k<T, 1>(a, gy, ldgy, g, gs != nullptr, gx, ldgx, part, grid, smem, TN, s, pa);
 }
 
 template <typename T>
@@ -1002,23 +1021,27 @@ cudaError_t csr_t(const LayerArgs& a, const void* gy, int64_t ldgy, int64_t in_d
 
 }  // namespace
 
-cudaError_t launch_logic_forward(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s) {
+cudaError_t launch_logic_forward(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s,
+                                 const PeerArgs* peers) {
+    const PeerArgs pa = peers ? *peers : PeerArgs{};
     switch (a.dtype) {
-        case CLB_F32: return fwd_t<float>(a, y, ldy, gs, s);
-        case CLB_F64: return fwd_t<double>(a, y, ldy, gs, s);
-        case CLB_BF16: return fwd_t<__nv_bfloat16>(a, y, ldy, gs, s);
-        case CLB_F16: return fwd_t<__half>(a, y, ldy, gs, s);
+        case CLB_F32: return fwd_t<float>(a, y, ldy, gs, s, pa);
+        case CLB_F64: return fwd_t<double>(a, y, ldy, gs, s, pa);
+        case CLB_BF16: return fwd_t<__nv_bfloat16>(a, y, ldy, gs, s, pa);
+        case CLB_F16: return fwd_t<__half>(a, y, ldy, gs, s, pa);
     }
     return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_logic_backward(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs* gs, void* gx,
-                                  int64_t ldgx, void* partials, int64_t part_chunks, cudaStream_t s) {
+                                  int64_t ldgx, void* partials, int64_t part_chunks, cudaStream_t s,
+                                  const PeerArgs* peers) {
+    const PeerArgs pa = peers ? *peers : PeerArgs{};
     switch (a.dtype) {
-        case CLB_F32: return bwd_t<float>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
-        case CLB_F64: return bwd_t<double>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
-        case CLB_BF16: return bwd_t<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
-        case CLB_F16: return bwd_t<__half>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s);
+        case CLB_F32: return bwd_t<float>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s, pa);
+        case CLB_F64: return bwd_t<double>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s, pa);
+        case CLB_BF16: return bwd_t<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s, pa);
+        case CLB_F16: return bwd_t<__half>(a, gy, ldgy, gs, gx, ldgx, partials, part_chunks, s, pa);
     }
     return cudaErrorInvalidValue;
 }
@@ -1044,7 +1067,7 @@ int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void*
             const int bv = bwd_vec_f32();
             const bool wide = vec && bv == 8 && bwd_wide_ok(a, gs ? 0 : ldgy, gs, ldgx);
             v = vec ? (bv == 2 ? 2 : wide ? 8 : 4) : 1;
-            lpn = bwd_lpn<float>(a, vec, v, gx);
+            lpn = bwd_lpn<float>(a, vec, v, gx, false);
             break;
         }
         case CLB_F64:
@@ -1054,12 +1077,12 @@ int64_t logic_backward_chunks(int dtype, int64_t ncols, int64_t ldx, const void*
         case CLB_BF16:
             vec = bwd_vec<__nv_bfloat16>(a, gy, ldgy, gs, gx, ldgx);
             v = vec ? vmax<__nv_bfloat16>() : 1;
-            lpn = bwd_lpn<__nv_bfloat16>(a, vec, v, gx);
+            lpn = bwd_lpn<__nv_bfloat16>(a, vec, v, gx, false);
             break;
         case CLB_F16:
             vec = bwd_vec<__half>(a, gy, ldgy, gs, gx, ldgx);
             v = vec ? vmax<__half>() : 1;
-            lpn = bwd_lpn<__half>(a, vec, v, gx);
+            lpn = bwd_lpn<__half>(a, vec, v, gx, false);
             break;
         default: return -1;
     }

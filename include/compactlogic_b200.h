@@ -219,6 +219,39 @@ int clb_logic_backward(int dtype, const void* x, int64_t ldx, int64_t ncols, con
 int clb_logic_grad_finalize(int dtype, const void* partials, int64_t nchunks, int64_t n_out, int64_t K,
                             int64_t group, int weight_mode, const void* weights, void* grad_w, clb_stream_t stream);
 
+/* ---- width-sharded (neuron-parallel) training, one process per GPU ----
+ * Each of n_peers ranks owns a contiguous share of a dense layer's neurons and every rank holds the
+ * full input activations.  The collectives are fused into the layer kernels over NVLink peer memory:
+ *  - forward: the neuron share's output rows are stored to every rank's full activation buffer,
+ *    y_peers[p] = rank p's buffer + (first owned neuron) * ldy (an all-gather in the epilogue);
+ *  - backward: grad_y of the owned neurons is the sum over ranks of their partial grad_x buffers of
+ *    the following layer, gy_peers[p] = rank p's partial + (first owned neuron) * ldgy (a
+ *    reduce-scatter in the grad_y load); grad_x is this rank's partial for the previous layer.
+ * The caller orders the ranks around each call (a barrier after it) so that no rank reads a buffer
+ * before every writer has finished.  y_peers / gy_peers are HOST arrays of n_peers <= 8 device
+ * pointers, all with the same address modulo 16; group is 1 (dense layers).  Otherwise as
+ * clb_logic_forward / clb_logic_backward (partials_chunks from clb_logic_backward_chunks with
+ * grad_y = gy_peers[0]).  The reference has no distributed code; these have no reference counterpart. */
+int clb_logic_forward_peers(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
+                            const int32_t* slots, int64_t n_out, int64_t K, int weight_mode, const void* weights,
+                            const uint8_t* gates, int has_pad, void* const* y_peers, int n_peers, int64_t ldy,
+                            clb_stream_t stream);
+int clb_logic_backward_peers(int dtype, const void* x, int64_t ldx, int64_t ncols, const int32_t* slots,
+                             int64_t n_out, int64_t K, int weight_mode, const void* weights, const uint8_t* gates,
+                             int has_pad, const void* const* gy_peers, int n_peers, int64_t ldgy, void* grad_x,
+                             int64_t ldgx, int zero_grad_x, int64_t in_features, void* partials,
+                             int64_t partials_chunks, clb_stream_t stream);
+
+/* Buffers shared between the ranks' processes: a device allocation of its own (cudaMalloc on the
+ * current device), its 64-byte IPC handle, and the mapping of another process's handle into this
+ * one (peer access enabled on first use). */
+#define CLB_IPC_HANDLE_BYTES 64
+int clb_peer_alloc(size_t bytes, void** ptr);
+int clb_peer_free(void* ptr);
+int clb_ipc_export(const void* ptr, void* handle);
+int clb_ipc_import(const void* handle, void** ptr);
+int clb_ipc_close(void* ptr);
+
 /* Layout helpers: dst[c, r] = src[r, c] for elem_bytes in {1,2,4,8}; fp32 <-> bf16 casts. */
 int clb_transpose(int elem_bytes, const void* src, int64_t rows, int64_t cols, int64_t ld_src, void* dst,
                   int64_t ld_dst, clb_stream_t stream);
