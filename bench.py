@@ -176,7 +176,8 @@ def bench_c2(args, dev, rank, world):
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.Adam(params, lr=0.01, fused=True)
     sync = None if width else GradAllReduce(params)
-    B = C2["batch"]
+    strong = args.strong and not width
+    B = C2["batch"] // world if strong else C2["batch"]
     x_host, y_host = c2_inputs(1000 + (0 if width else rank), B)
     x_dev, y_dev = x_host.to(dev), y_host.to(dev)
 
@@ -224,16 +225,17 @@ def bench_c2(args, dev, rank, world):
         achieved = tot_b / (tot_ms / 1e3) / 1e9
         roof = {"kernel": f"logic_{dom}_kernel", "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                 "peak_source": src, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                "traffic": NCU_TRAFFIC.get(f"logic_{dom}_kernel") if C2["layers"] == 6 else None,
+                "traffic": NCU_TRAFFIC.get(f"logic_{dom}_kernel") if C2["layers"] == 6 and B == 1024 and not width else None,
                 "traffic_note": "ncu dram__bytes_read+write per launch, cold cache (profiles/)",
                 "algorithmic_bytes_per_launch": round(tot_b / n), "launches": n, "avg_ms": round(tot_ms / n, 4),
                 "shares": {k: round(v[1] / sum(w[1] for w in kern.values()), 3) for k, v in kern.items()}}
     step_bytes = c2_bytes_per_step(B)
-    gb = B if width else B * world
+    gb = B if width else B * world  # strong DP: B = 1024 / world, so gb = 1024
     res = {
         "metric": "train_samples_per_s", "value": round(gb / (ms / 1e3), 1), "unit": "samples/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "strong" if width else "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong" if (width or strong) else "weak", "vs_baseline": None,
+        "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": f"c2: 784 -> {C2['layers']}x LogicLayer(64000, K=16) -> GroupSum(10, tau=10); CE, "
                                + ("width-sharded neurons, peer-fused gather / reduce-scatter" if width else
@@ -537,6 +539,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-refcuda", action="store_true", help="skip the reference-CUDA-kernel step timing")
     ap.add_argument("--chunk-words", type=int, default=128)
+    ap.add_argument("--strong", action="store_true",
+                    help="c2 data parallel with the global batch fixed at 1024 (1024/N per GPU)")
     ap.add_argument("--parallel", default="dp", choices=["dp", "width"],
                     help="c2 multi-GPU scheme: data parallel (default) or width-sharded neurons")
     ap.add_argument("--layers", type=int, default=None, help="override the c2 depth (profiling on a smaller case)")
