@@ -478,6 +478,17 @@ def bench_c4(args, dev, rank, world, chunk_words):
         ch.copy_(c, non_blocking=True)
 
     ms_e2e = timed(e2e, steps, 1, dev)
+    pruned = None
+    if not args.no_prune:
+        # the same network after the compiler's stage-1 pruning: fewer gates, identical counts
+        pnet = cl.PackedLogicNet(model, chunk_words=chunk_words, prune="exact")
+        pcounts = torch.zeros_like(counts)
+        ms_p = timed(lambda: pnet.counts_packed(xw, n, pcounts), steps, 1, dev)
+        pruned = {"value": round(evals / (ms_p / 1e3), 1), "unit": "network gate-evals/s",
+                  "ms_per_step": round(ms_p, 3), "gates": pnet.prune_stats["gates"],
+                  "kept_gates": pnet.prune_stats["kept"], "counts_equal_unpruned": bool(torch.equal(pcounts, counts)),
+                  "note": "value counts the unpruned network's gates; the kernels evaluate only the kept ones"}
+        del pnet
     # roofline of the packed layer kernel: time one chunk's layer launches with events
     hbm, src = peaks()
     bytes_model = (8 * W * (C4["in_dim"] + C4["width"]) + C4["width"] * 9 +
@@ -492,12 +503,13 @@ def bench_c4(args, dev, rank, world, chunk_words):
         "roofline": {"kernel": "packed layer chain (all launches of one pass)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm, "peak_source": src, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
-                     "note": "L2-resident chunk schedule: the byte model counts each layer's activations as an "
-                             "HBM round trip; frac > 1 means the chunk stayed in L2"},
+                     "note": "byte model: every layer's activations make one HBM round trip (128-word chunks "
+                             "stream through HBM); frac > 1 would mean a chunk stayed in L2"},
         "clocks": clk.summary(),
         "e2e": {"value": round(evals / (ms_e2e / 1e3), 1), "unit": "gate-evals/s",
                 "h2d_bytes_per_step": xh.numel() * 8, "d2h_bytes_per_step": ch.numel() * 4},
         "gpu_launches": int(launches),
+        "pruned": pruned,
     }, model
 
 
@@ -539,6 +551,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-refcuda", action="store_true", help="skip the reference-CUDA-kernel step timing")
     ap.add_argument("--chunk-words", type=int, default=128)
+    ap.add_argument("--no-prune", action="store_true", help="skip the pruned packed-inference sub-measurement")
     ap.add_argument("--strong", action="store_true",
                     help="c2 data parallel with the global batch fixed at 1024 (1024/N per GPU)")
     ap.add_argument("--parallel", default="dp", choices=["dp", "width"],

@@ -31,9 +31,11 @@ class PackedLogicNet:
 
     forward(x) -> int32 class counts [batch, k]; logits(x) = counts / tau, equal to the reference
     eval-mode output; predict(x) = argmax (first maximum, as torch.argmax).
+    prune: None, or "exact" / "reference" to evaluate the network after the compiler's stage-1 pruning
+    (same counts, fewer gates; see compactlogic_b200.prune).
     """
 
-    def __init__(self, model: torch.nn.Module, device=None, chunk_words: int = 128):
+    def __init__(self, model: torch.nn.Module, device=None, chunk_words: int = 128, prune: Optional[str] = None):
         mods = list(model)
         if not mods or not isinstance(mods[-1], GroupSum):
             raise ValueError("PackedLogicNet needs a model ending in GroupSum")
@@ -57,6 +59,7 @@ class PackedLogicNet:
                 raise ValueError("PackedLogicNet: layer widths do not chain")
         self.in_features = self.layers[0].in_features
         self.class_size = -(-self.layers[-1].n_out // self.k)
+        self.plan = self._prune_plan(model, prune) if prune else None
         self._bufs = None
         self._ws = None
         self.use_graphs = True
@@ -74,6 +77,35 @@ class PackedLogicNet:
                spec.group, L.ptr(sel_ab), L.ptr(sel_gate), L.stream(self.device))
         in_features = spec.in_features
         return _Frozen(sel_ab, sel_gate, n_out, in_features)
+
+    @torch.no_grad()
+    def _prune_plan(self, model, keep: str):
+        """Simplify the frozen network first (the compiler's stage-1 pruning, compiler/prune.py:298-310)
+        and evaluate only the gates that survive: every kept gate of the inner layers is a row of one
+        signal buffer (inputs first), so rewired operands may read any earlier row; the last layer
+        becomes the fused count layer with pass-throughs, inverters and constants in place of the
+        simplified neurons.  Counts are identical to the unpruned network's."""
+        import numpy as np
+        from .prune import packed_plan, prune_circuit
+        raw = []
+        for m in model:
+            if not isinstance(m, LogicLayer):
+                continue
+            spec = m._layer_spec(self.device)
+            slots = spec.slots.cpu().numpy()
+            sel = m._selected().cpu().numpy().astype(np.int64)
+            gates = spec.gates.cpu().numpy().astype(np.int64)
+            j = np.arange(spec.n_out)
+            r = j // spec.group
+            raw.append((slots[j, sel[r], 0].astype(np.int64), slots[j, sel[r], 1].astype(np.int64), gates[r, sel[r]]))
+        pc = prune_circuit(raw, self.in_features, self.k, keep=keep)
+        layers, (cab, cg), rows = packed_plan(pc)
+        dev = self.device
+        t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a)).to(dev, dt)
+        self.prune_stats = {"gates": int(sum(len(g) for _, _, g in raw)), "kept": pc.bop_count,
+                            "rows": int(rows), "keep": keep}
+        return {"layers": [(t(ab, torch.int32), t(g, torch.uint8), len(g)) for ab, g in layers],
+                "count": (t(cab, torch.int32), t(cg, torch.uint8), len(cg)), "rows": int(rows)}
 
     # ------------------------------------------------------------------
     def pack(self, x: torch.Tensor) -> torch.Tensor:
@@ -128,8 +160,39 @@ class PackedLogicNet:
             self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
         return self._ws
 
+    def _run_pruned(self, xw: torch.Tensor, batch: int, counts: torch.Tensor) -> None:
+        W = xw.shape[1]
+        cw = max(1, min(self.chunk_words, W))
+        plan = self.plan
+        if self._bufs is None or self._bufs[0].shape[1] < cw:
+            self._bufs = (torch.empty(plan["rows"], cw, dtype=torch.int64, device=self.device),)
+        sig = self._bufs[0]
+        ld = sig.stride(0)
+        s = L.stream(self.device)
+        counts.zero_()
+        n = 0
+        cab, cg, n_out = plan["count"]
+        for w0 in range(0, W, cw):
+            nw = min(cw, W - w0)
+            sig[:self.in_features, :nw].copy_(xw[:, w0:w0 + nw])
+            row = self.in_features
+            for ab, g, m in plan["layers"]:
+                if m:
+                    L.call("clb_packed_layer", L.ptr(sig), ld, nw, L.ptr(ab), L.ptr(g), m, L.ptr(sig) + 8 * row * ld,
+                           ld, s)
+                    n += 1
+                row += m
+            nsamp = min(64 * nw, batch - 64 * w0)
+            ws = self._count_ws(nw)
+            L.call("clb_packed_layer_count", L.ptr(sig), ld, nw, L.ptr(cab), L.ptr(cg), n_out, self.k,
+                   self.class_size, L.ptr(counts), 64 * w0, nsamp, L.ptr(ws), ws.numel(), s)
+            n += 1
+        self.launches_per_pass = n
+
     def _run(self, xw: torch.Tensor, batch: int, counts: torch.Tensor) -> None:
         """Enqueue one pass: per chunk, every layer then the fused last layer + class count."""
+        if self.plan is not None:
+            return self._run_pruned(xw, batch, counts)
         W = xw.shape[1]
         cw = max(1, min(self.chunk_words, W))
         bufs = self._buffers(cw)
@@ -205,7 +268,7 @@ def _state_prefixes(state):
 
 
 def packed_from_state_dict(state: dict, input_dim: int, k: int, tau: float = 1.0, device="cuda",
-                           chunk_words: int = 128) -> PackedLogicNet:
+                           chunk_words: int = 128, prune: Optional[str] = None) -> PackedLogicNet:
     """PackedLogicNet straight from a checkpoint's ``model_state`` of dense logic layers (the layout the
     reference writes, experiments/experiment_script.py:520-541, and its compiler reads,
     compiler/extract.py:49-98): per layer ``{i}.weights`` (out, K), ``{i}.indices`` (2, out, K),
@@ -230,4 +293,5 @@ def packed_from_state_dict(state: dict, input_dim: int, k: int, tau: float = 1.0
         in_dim = out
     if not layers:
         raise ValueError("no dense logic layers in the state dict")
-    return PackedLogicNet(torch.nn.Sequential(*layers, GroupSum(k, tau)), device=device, chunk_words=chunk_words)
+    return PackedLogicNet(torch.nn.Sequential(*layers, GroupSum(k, tau)), device=device, chunk_words=chunk_words,
+                          prune=prune)

@@ -15,7 +15,11 @@ Fixtures written (all small, npz):
                       random boolean inputs, and the class counts of the reference CPU circuit
                       evaluator (simulation/consistency.py:80-130 on compiler/extract.py:200-268);
   freezer_trace.json  freeze steps of SequentialEntropyFreezer / FixedSequentialEntropyFreezer on a
-                      scripted entropy schedule.
+                      scripted entropy schedule;
+  pruned.npz          the reference compiler's stage-1 pruning (compiler/prune.py naive_prune_circuit) of
+                      the discrete.npz network and of a 784 -> 300 -> 200 network dominated by constant /
+                      pass-through / inverter gates with repeated operands: kept gates (node id, gate id,
+                      operand signal ids) and every class-group source (constant, signal, inversion).
 
 Usage: python tests/golden/make_golden.py [--ref /root/reference]
 """
@@ -170,6 +174,58 @@ def discrete(cl):
     np.savez_compressed(os.path.join(HERE, "discrete.npz"), **out)
 
 
+def _prune_record(circuit, tag, out):
+    from compiler.prune import naive_prune_circuit
+    pc = naive_prune_circuit(circuit)
+    out[f"{tag}.node"] = np.array([n.node_id for n in pc.nodes], np.int64)
+    out[f"{tag}.gate"] = np.array([n.gate_id for n in pc.nodes], np.int64)
+    out[f"{tag}.a"] = np.array([n.input_a.signal_id for n in pc.nodes], np.int64)
+    out[f"{tag}.b"] = np.array([n.input_b.signal_id for n in pc.nodes], np.int64)
+    kind, sig, inv = [], [], []
+    for group in pc.class_groups:
+        for src in group:
+            if src.const_value is not None:
+                kind.append(src.const_value)
+                sig.append(-1)
+                inv.append(0)
+            else:
+                kind.append(2)
+                sig.append(src.signal_id)
+                inv.append(int(src.inverted))
+    shape = (pc.num_classes, -1)
+    out[f"{tag}.src_kind"] = np.array(kind, np.int64).reshape(shape)
+    out[f"{tag}.src_sig"] = np.array(sig, np.int64).reshape(shape)
+    out[f"{tag}.src_inv"] = np.array(inv, np.int64).reshape(shape)
+
+
+def pruned(cl):
+    import compiler.extract as ce
+    out = {}
+    d = np.load(os.path.join(HERE, "discrete.npz"))
+    state = {f"{i}.{n}": torch.from_numpy(d[f"{i}.{n}"]) for i in range(1, 4)
+             for n in ("weights", "indices", "gate_sequence")}
+    circuit = ce.extract_circuit_from_state(state, args=None, num_classes=10, tau=3.0, metadata={"dataset": "mnist"})
+    _prune_record(circuit, "d", out)
+    # trivial-heavy network: gates mostly constants / pass-throughs / inverters, many a == b operands
+    g = torch.Generator().manual_seed(9)
+    widths = [784, 300, 200]
+    pool = torch.tensor([0, 15, 3, 5, 10, 12, 3, 5, 1, 6, 7, 9, 14, 2, 4, 8, 11, 13], dtype=torch.uint8)
+    state = {}
+    for i in range(2):
+        n_in, n_out, K = widths[i], widths[i + 1], 4
+        idx = torch.randint(0, n_in, (2, n_out, K), generator=g)
+        same = torch.rand((n_out, K), generator=g) < 0.2
+        idx[1][same] = idx[0][same]
+        state[f"{i + 1}.weights"] = torch.randn((n_out, K), generator=g)
+        state[f"{i + 1}.indices"] = idx
+        state[f"{i + 1}.gate_sequence"] = pool[torch.randint(0, len(pool), (n_out, K), generator=g)]
+    for key, t in state.items():
+        out["t." + key] = t.numpy()
+    circuit = ce.extract_circuit_from_state(state, args=None, num_classes=10, tau=1.0, metadata={"dataset": "mnist"})
+    _prune_record(circuit, "t", out)
+    np.savez_compressed(os.path.join(HERE, "pruned.npz"), **out)
+
+
 def freezer_trace(cl):
     class Fake(torch.nn.Module):
         def __init__(self, rows):
@@ -217,6 +273,7 @@ def main():
     big_layer_sha(cl)
     discrete(cl)
     freezer_trace(cl)
+    pruned(cl)
     print("fixtures written to", HERE)
 
 

@@ -70,6 +70,8 @@ def test_c4_full_network_packed_equals_float_eval():
     model = torch.nn.Sequential(*layers, cl.GroupSum(10, 1.0)).cuda().eval()
     x = (torch.rand(4096, 784, device="cuda") < 0.5).float()
     counts = cl.PackedLogicNet(model)(x)
+    pruned = cl.PackedLogicNet(model, prune="exact")
+    assert torch.equal(pruned(x), counts) and pruned.prune_stats["kept"] < pruned.prune_stats["gates"]
     with torch.no_grad():
         float_counts = torch.round(model(x)).to(torch.int32)
     assert torch.equal(counts, float_counts)

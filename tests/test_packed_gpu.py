@@ -107,3 +107,33 @@ def test_fused_threshold_packing(B):
     np.testing.assert_array_equal(net.pack_raw(px.cuda(), 3).cpu().numpy().view(np.uint64),
                                   O.pack_samples(binar.reshape(B, -1).numpy()))
     np.testing.assert_array_equal(net.forward_raw(px.cuda(), 3).cpu().numpy(), net(binar.cuda()).cpu().numpy())
+
+
+@pytest.mark.parametrize("keep", ["exact", "reference"])
+@pytest.mark.parametrize("chunk_words", [1, 32])
+def test_pruned_packed_net_matches_reference_circuit(golden, keep, chunk_words):
+    """After the compiler's stage-1 pruning the packed network still gives the reference evaluator's
+    counts, with fewer gates (reference liveness: the compiler's BOP count, tests/golden/pruned.npz)."""
+    d = golden("discrete.npz")
+    net = cl.PackedLogicNet(_model_from_fixture(d), chunk_words=chunk_words, prune=keep)
+    np.testing.assert_array_equal(net(cuda(d["x"].astype(np.float32))).cpu().numpy(), d["counts"])
+    assert net.prune_stats["gates"] == 1200
+    if keep == "reference":
+        assert net.prune_stats["kept"] == len(golden("pruned.npz")["d.node"])
+    else:
+        assert net.prune_stats["kept"] <= len(golden("pruned.npz")["d.node"])
+
+
+def test_pruned_conv_net_and_checkpoint(golden):
+    torch.manual_seed(3)
+    model = torch.nn.Sequential(cl.ConvLayer((3, 8, 8), 1, 16, 3, 2, num_gates=8),
+                                cl.ConvLayer((16, 4, 4), 1, 32, 3, 2, num_gates=8), torch.nn.Flatten(),
+                                cl.LogicLayer(128, 100, num_gates=8), cl.GroupSum(5, 2.0)).cuda().eval()
+    x = (torch.rand(300, 3, 8, 8, device="cuda") < 0.5).float()
+    counts = cl.PackedLogicNet(model, chunk_words=2, prune="exact")(x)
+    np.testing.assert_array_equal(counts.cpu().numpy(), torch.round(model(x) * 2.0).to(torch.int32).cpu().numpy())
+    d = golden("discrete.npz")
+    state = {f"{i}.{n}": torch.from_numpy(d[f"{i}.{n}"]) for i in range(1, 4) for n in ("weights", "indices",
+                                                                                           "gate_sequence")}
+    net = cl.packed_from_state_dict(state, input_dim=784, k=int(d["k"]), tau=float(d["tau"]), prune="exact")
+    np.testing.assert_array_equal(net(cuda(d["x"].astype(np.float32))).cpu().numpy(), d["counts"])
