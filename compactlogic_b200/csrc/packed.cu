@@ -238,6 +238,68 @@ packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords,
     }
 }
 
+// Persistent variant: a grid of about one wave strides over the neuron tiles, and each warp loads the
+// tables of its next tile while the operand words of the current one are in flight, so a tile costs one
+// memory round trip instead of two (tables, then operands) plus a CTA launch.
+template <int R, int V, int MINB = 1>
+__global__ void __launch_bounds__(256, MINB)
+packed_layer_pipe_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
+                         const uint8_t* __restrict__ sel_gate, int64_t n_out, uint64_t* __restrict__ y, int64_t ldy,
+                         int tw_log2) {
+    using Vw = Vec<uint64_t, V>;
+    const int TW = 1 << tw_log2;
+    const int lane = threadIdx.x & 31;
+    const int64_t w = ((int64_t)blockIdx.x * TW + (lane & (TW - 1))) * V;
+    const int64_t npw = 32 >> tw_log2;
+    const int64_t warp_global = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) >> 5;
+    const int64_t stride = (((int64_t)gridDim.y * blockDim.x) >> 5) * npw * R;
+    if (w >= nwords) return;
+    const int64_t sub = lane >> tw_log2;
+    int64_t base = warp_global * npw * R;
+    int2 ab[R];
+    int g[R];
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+        const int64_t j = base + q * npw + sub;
+        ab[q] = j < n_out ? sel_ab[j] : make_int2(-1, -1);
+        g[q] = j < n_out ? sel_gate[j] : 0;
+    }
+    for (; base < n_out; base += stride) {
+        Vw va[R], vb[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) va[q].v[i] = vb[q].v[i] = 0;
+            if (ab[q].x >= 0) va[q] = *reinterpret_cast<const Vw*>(x + (int64_t)ab[q].x * ldx + w);
+            if (ab[q].y >= 0) vb[q] = *reinterpret_cast<const Vw*>(x + (int64_t)ab[q].y * ldx + w);
+        }
+        int gc[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            gc[q] = g[q];
+            const int64_t j = base + stride + q * npw + sub;
+            ab[q] = j < n_out ? sel_ab[j] : make_int2(-1, -1);
+            g[q] = j < n_out ? sel_gate[j] : 0;
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int64_t j = base + q * npw + sub;
+            if (j < n_out) {
+                Vw o;
+#pragma unroll
+                for (int i = 0; i < V; ++i) o.v[i] = gate_word<uint64_t>(gc[q], va[q].v[i], vb[q].v[i]);
+                *reinterpret_cast<Vw*>(y + j * ldy + w) = o;
+            }
+        }
+    }
+}
+
+int sm_count() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
 // ------------------------------------------------------------------------------------------
 // Packed GroupSum: counts[(sample0 + 64 w + i) * k + c] += #{rows r of class c : bit i of word(r, w)}.
 // A CTA owns one class, a tile of TW word columns and S = 256/TW row segments of up to 240 rows:
@@ -488,6 +550,17 @@ int packed_env(const char* name, int dflt) {
 template <int R, int V>
 void packed_layer_go(dim3 grid, cudaStream_t s, int minb, const uint64_t* x, int64_t ldx, int64_t nwords, const int2* ab,
                      const uint8_t* g, int64_t n_out, uint64_t* y, int64_t ldy, int tw_log2) {
+    static const int pipe = packed_env("CLB_PACKED_PIPE", 1);
+    if (pipe > 0) {
+        // about `pipe` waves of resident CTAs, striding over the tiles
+        const int64_t cap = std::max<int64_t>(1, (int64_t)sm_count() * (minb == 4 ? 4 : 2) * pipe / grid.x);
+        grid.y = (unsigned)std::min<int64_t>(grid.y, cap);
+        if (minb == 4)
+            packed_layer_pipe_kernel<R, V, 4><<<grid, 256, 0, s>>>(x, ldx, nwords, ab, g, n_out, y, ldy, tw_log2);
+        else
+            packed_layer_pipe_kernel<R, V, 1><<<grid, 256, 0, s>>>(x, ldx, nwords, ab, g, n_out, y, ldy, tw_log2);
+        return;
+    }
     if (minb == 4)
         packed_layer_kernel<R, V, 4><<<grid, 256, 0, s>>>(x, ldx, nwords, ab, g, n_out, y, ldy, tw_log2);
     else
@@ -497,7 +570,9 @@ void packed_layer_go(dim3 grid, cudaStream_t s, int minb, const uint64_t* x, int
 cudaError_t launch_packed_layer(const uint64_t* x, int64_t ldx, int64_t nwords, const int32_t* sel_ab,
                                 const uint8_t* sel_gate, int64_t n_out, uint64_t* y, int64_t ldy, cudaStream_t s) {
     if (n_out == 0 || nwords == 0) return cudaSuccess;
-    static const int R = packed_env("CLB_PACKED_R", 4);
+    // default: the persistent table-prefetching kernel with 2 neurons per thread (measured best: c4 pass
+    // 406.8 ms vs 438.2 ms for the one-shot kernel with 4); CLB_PACKED_PIPE=0 selects the one-shot kernel
+    static const int R = packed_env("CLB_PACKED_R", packed_env("CLB_PACKED_PIPE", 1) > 0 ? 2 : 4);
     static const int minb = packed_env("CLB_PACKED_MINB", 4);
     const bool v2 = nwords % 2 == 0 && ldx % 2 == 0 && ldy % 2 == 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0;
     const int V = v2 ? 2 : 1;
