@@ -34,17 +34,21 @@ constexpr int kWarps = kThreads / 32;
 template <typename A> struct A4 { A x, y, z, w; };
 
 // Shared-memory slot stage for TN neurons.
+// Forward: each neuron's entries are compacted, two-operand gates first (ns of them: ab, p*c1, p*c2,
+// p*c3), then one-operand gates (n1 of them: the used operand in ab.x and its coefficient p*c1 or p*c2
+// in cf.x); constant gates only contribute to c0.  Backward: entry k is slot k (ns = K).
 template <typename A> struct Stage {
-    A4<A>* cf;   // [TN*K] forward: p*c1, p*c2, p*c3 ; backward: c0, c1, c2, c3 (raw)
+    A4<A>* cf;   // [TN*K] forward: see above ; backward: c0, c1, c2, c3 (raw)
     int2* ab;    // [TN*K]
     A* p;        // [TN*K] backward only
     A* c0;       // [TN]   forward: sum_k p*c0
-    int* ns;     // [TN]   number of active slots
+    int* ns;     // [TN]   forward: two-operand entries; backward: slots
+    int* n1;     // [TN]   forward: one-operand entries
 };
 
 template <typename A>
 __host__ __device__ inline size_t stage_bytes(int TN, int K, bool backward) {
-    size_t b = (size_t)TN * K * (sizeof(A4<A>) + sizeof(int2)) + (size_t)TN * (sizeof(A) + sizeof(int));
+    size_t b = (size_t)TN * K * (sizeof(A4<A>) + sizeof(int2)) + (size_t)TN * (sizeof(A) + 2 * sizeof(int));
     if (backward) b += (size_t)TN * K * sizeof(A);
     return b;
 }
@@ -59,6 +63,7 @@ __device__ __forceinline__ Stage<A> carve(unsigned char* smem, int TN, int K, bo
     if (backward) after += (size_t)TN * K;
     s.c0 = after;
     s.ns = reinterpret_cast<int*>(s.c0 + TN);
+    s.n1 = s.ns + TN;
     return s;
 }
 
@@ -69,6 +74,21 @@ __device__ __forceinline__ int2 used_operands(int2 s, const GatePoly& gp) {
     if (gp.c1 == 0.f && gp.c3 == 0.f) s.x = -1;
     if (gp.c2 == 0.f && gp.c3 == 0.f) s.y = -1;
     return s;
+}
+
+// Forward entry of one slot: 2 = two-operand gate, 1 = one-operand gate (operand moved to .x),
+// 0 = constant gate (contributes p*c0 only).
+template <typename A>
+__device__ __forceinline__ int fwd_entry(int2 s, const GatePoly& gp, A p, int2& ab, A4<A>& cf) {
+    const bool ua = gp.c1 != 0.f || gp.c3 != 0.f, ub = gp.c2 != 0.f || gp.c3 != 0.f;
+    if (ua && ub) {
+        ab = s;
+        cf = A4<A>{p * (A)gp.c1, p * (A)gp.c2, p * (A)gp.c3, (A)0};
+        return 2;
+    }
+    ab = make_int2(ua ? s.x : s.y, -1);
+    cf = A4<A>{p * (A)(ua ? gp.c1 : gp.c2), (A)0, (A)0, (A)0};
+    return (ua || ub) ? 1 : 0;
 }
 
 __device__ __forceinline__ float exp_acc(float v) { return expf(v); }
@@ -115,27 +135,42 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
                 p = w[r * K + k];
             }
             GatePoly gp{0.f, 0.f, 0.f, 0.f};
-            if (valid) {
-                gp = gate_poly(a.gates[r * K + k] & 15);
-                st.ab[e] = used_operands(slots[j * K + k], gp);
-                if (BACKWARD) {
+            if (valid) gp = gate_poly(a.gates[r * K + k] & 15);
+            if (BACKWARD) {
+                if (valid) {
+                    st.ab[e] = used_operands(slots[j * K + k], gp);
                     st.cf[e] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
                     st.p[e] = p;
-                } else {
-                    st.cf[e] = A4<A>{p * (A)gp.c1, p * (A)gp.c2, p * (A)gp.c3, (A)0};
                 }
-            }
-            const A c0sum = seg_sum(p * (A)gp.c0, K);
-            if (e < total && k == 0) {
-                st.ns[t] = valid ? K : 0;
-                if (!BACKWARD) st.c0[t] = c0sum;
+                if (e < total && k == 0) st.ns[t] = valid ? K : 0;
+            } else {
+                int2 ab;
+                A4<A> cf;
+                const int cls = valid ? fwd_entry(slots[j * K + k], gp, p, ab, cf) : 0;
+                // compact the K lanes of this neuron: two-operand entries first, then one-operand ones
+                const unsigned pm = __ballot_sync(0xffffffffu, cls == 2), om = __ballot_sync(0xffffffffu, cls == 1);
+                const int lane = threadIdx.x & 31;
+                const unsigned seg = K == 32 ? 0xffffffffu : (((1u << K) - 1u) << (lane & ~(K - 1)));
+                const unsigned below = seg & ((1u << lane) - 1u);
+                const int np = __popc(pm & seg), n1 = __popc(om & seg);
+                if (cls != 0) {
+                    const int pos = cls == 2 ? __popc(pm & below) : np + __popc(om & below);
+                    st.ab[t * K + pos] = ab;
+                    st.cf[t * K + pos] = cf;
+                }
+                const A c0sum = seg_sum(p * (A)gp.c0, K);
+                if (e < total && k == 0) {
+                    st.ns[t] = valid ? np : 0;
+                    st.n1[t] = valid ? n1 : 0;
+                    st.c0[t] = c0sum;
+                }
             }
         }
         return;
     }
     for (int t = threadIdx.x; t < TN; t += blockDim.x) {
         const int64_t j = j0 + t;
-        int ns = 0;
+        int ns = 0, n1 = 0;
         A c0sum = 0;
         if (j < a.n_out) {
             const int64_t r = j / a.group;
@@ -144,15 +179,17 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
                 const int k = a.select[r];
                 if (k < K) {
                     const GatePoly gp = gate_poly(g[k] & 15);
-                    st.ab[t * K] = used_operands(slots[j * K + k], gp);
                     if (BACKWARD) {
+                        st.ab[t * K] = used_operands(slots[j * K + k], gp);
                         st.cf[t * K] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
                         st.p[t * K] = (A)1;
+                        ns = 1;
                     } else {
-                        st.cf[t * K] = A4<A>{(A)gp.c1, (A)gp.c2, (A)gp.c3, (A)0};
+                        const int cls = fwd_entry(slots[j * K + k], gp, (A)1, st.ab[t * K], st.cf[t * K]);
+                        ns = cls == 2 ? 1 : 0;
+                        n1 = cls == 1 ? 1 : 0;
                         c0sum = (A)gp.c0;
                     }
-                    ns = 1;
                 }
             } else {
                 const A* wr = w != nullptr ? w + r * K : nullptr;
@@ -163,23 +200,43 @@ __device__ void fill_stage(const LayerArgs& a, int64_t j0, int TN, Stage<A> st) 
                     sum = 0;
                     for (int k = 0; k < K; ++k) sum += exp_acc(wr[k] - m);
                 }
-                for (int k = 0; k < K; ++k) {
-                    const A p = a.mode == CLB_W_LOGITS ? exp_acc(wr[k] - m) / sum : (w != nullptr ? wr[k] : (A)0);
-                    const GatePoly gp = gate_poly(g[k] & 15);
-                    st.ab[t * K + k] = used_operands(slots[j * K + k], gp);
-                    if (BACKWARD) {
+                if (BACKWARD) {
+                    for (int k = 0; k < K; ++k) {
+                        const A p = a.mode == CLB_W_LOGITS ? exp_acc(wr[k] - m) / sum : (w != nullptr ? wr[k] : (A)0);
+                        const GatePoly gp = gate_poly(g[k] & 15);
+                        st.ab[t * K + k] = used_operands(slots[j * K + k], gp);
                         st.cf[t * K + k] = A4<A>{(A)gp.c0, (A)gp.c1, (A)gp.c2, (A)gp.c3};
                         st.p[t * K + k] = p;
-                    } else {
-                        st.cf[t * K + k] = A4<A>{p * (A)gp.c1, p * (A)gp.c2, p * (A)gp.c3, (A)0};
+                    }
+                    ns = K;
+                } else {
+                    for (int k = 0; k < K; ++k) {
+                        const GatePoly gp = gate_poly(g[k] & 15);
+                        ns += (gp.c1 != 0.f || gp.c3 != 0.f) && (gp.c2 != 0.f || gp.c3 != 0.f);
+                    }
+                    int ip = 0, io = ns;
+                    for (int k = 0; k < K; ++k) {
+                        const A p = a.mode == CLB_W_LOGITS ? exp_acc(wr[k] - m) / sum : (w != nullptr ? wr[k] : (A)0);
+                        const GatePoly gp = gate_poly(g[k] & 15);
+                        int2 ab;
+                        A4<A> cf;
+                        const int cls = fwd_entry(slots[j * K + k], gp, p, ab, cf);
+                        if (cls != 0) {
+                            const int pos = cls == 2 ? ip++ : io++;
+                            st.ab[t * K + pos] = ab;
+                            st.cf[t * K + pos] = cf;
+                        }
                         c0sum += p * (A)gp.c0;
                     }
+                    n1 = io - ns;
                 }
-                ns = K;
             }
         }
         st.ns[t] = ns;
-        if (!BACKWARD) st.c0[t] = c0sum;
+        if (!BACKWARD) {
+            st.n1[t] = n1;
+            st.c0[t] = c0sum;
+        }
     }
 }
 
@@ -230,7 +287,7 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
 #pragma unroll
         for (int i = 0; i < VEC; ++i) acc[i] = c0;
         if (active) {
-            const int ns = st.ns[t];
+            const int ns = st.ns[t], n1 = st.n1[t];
             const int2* ab = st.ab + t * K;
             const A4<A>* cf = st.cf + t * K;
 #pragma unroll 4
@@ -246,6 +303,15 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
                     acc[i] = fma(c.x, va[i], acc[i]);
                     acc[i] = fma(u, vb[i], acc[i]);
                 }
+            }
+#pragma unroll 4
+            for (int s = ns; s < ns + n1; ++s) {  // one-operand gates: acc += p*c * operand
+                const int idx = ab[s].x;
+                const A c = cf[s].x;
+                A va[VEC];
+                gather<T, VEC>(x, idx, a.ldx, col, va);
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) acc[i] = fma(c, va[i], acc[i]);
             }
         }
         if (!use_gs) {
@@ -440,7 +506,7 @@ logic_forward_narrow_kernel(const LayerArgs a, T* __restrict__ y, const int64_t 
 #pragma unroll
         for (int i = 0; i < VEC; ++i) acc[i] = c0;
         if (active) {
-            const int ns = st.ns[t];
+            const int ns = st.ns[t], n1 = st.n1[t];
             const int2* ab = st.ab + t * K;
             const A4<A>* cf = st.cf + t * K;
 #pragma unroll 4
@@ -456,6 +522,15 @@ logic_forward_narrow_kernel(const LayerArgs a, T* __restrict__ y, const int64_t 
                     acc[i] = fma(c.x, va[i], acc[i]);
                     acc[i] = fma(u, vb[i], acc[i]);
                 }
+            }
+#pragma unroll 4
+            for (int s = ns; s < ns + n1; ++s) {  // one-operand gates: acc += p*c * operand
+                const int idx = ab[s].x;
+                const A c = cf[s].x;
+                A va[VEC];
+                gather<T, VEC>(x, idx, a.ldx, col, va);
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) acc[i] = fma(c, va[i], acc[i]);
             }
         }
         if (!use_gs) {
