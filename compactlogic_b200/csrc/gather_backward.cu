@@ -1,0 +1,538 @@
+// Gather-form fused backward of a logic layer: destination-sorted, no scatter reductions.
+//
+// The scatter backward (logic_layer.cu) walks slots and adds each slot's activation gradient into
+// grad_x with L2 reductions.  Here the work is walked by destination instead: a per-layer index lists,
+// for every input feature i, the slot operands that read it ("occurrences", sorted by slot, so the
+// summation order is fixed for a given index).  One warp owns one input row and one column chunk;
+// for each occurrence it gathers the other operand's row and grad_y of the slot's neuron, and
+//   grad_x[i, n]        += p * (c_self + c3 * x_other) * gy[j, n]       (difflogic_kernel.cu:140-194)
+//   d loss / d p[j, k]  = sum_n gy[j, n] * f(a, b)                      (difflogic_kernel.cu:82-137)
+// the second written by exactly one occurrence per slot (its "owner"), into the same per-chunk
+// partials [nchunks, n_out, K] the scatter backward produces, so clb_logic_grad_finalize folds both.
+// grad_x is stored once per element (no pre-zeroing, no atomics).
+//
+// Occurrence record: int2 {other operand row or -1, meta}, meta = slot << 7 | zero << 6 | owner << 5 |
+// side << 4 | gate id.  side 0 = the occurrence is operand a of the slot, 1 = operand b.  Operands a
+// gate ignores get no occurrence (and read as -1 when they are the other operand).  A slot with no
+// occurrence at all (a constant gate, or every used operand is zero padding) still needs its
+// d loss / d p = c0 * sum_n gy[j, n]: it gets one "virtual" occurrence on row j % in_features with
+// the zero flag set, which evaluates the gate with its own operand read as 0 and adds nothing to
+// grad_x.
+//
+// Index layout (bytes, each part 256-aligned): starts int32 [in + 1], tmp int2 [2 * n_out * K] (the
+// unsorted fill), recs int2 [2 * n_out * K], cursor int32 [in].
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "gates.cuh"
+#include "kernels.h"
+
+namespace clb {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int64_t kMaxSlots = int64_t(1) << 24;  // slot id field of the record
+
+size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct IndexParts {
+    int32_t* starts;
+    int2* tmp;
+    int2* recs;
+    int32_t* cursor;
+    size_t bytes;
+};
+
+IndexParts index_parts(void* base, int64_t n_out, int64_t K, int64_t in_features) {
+    IndexParts p{};
+    unsigned char* b = reinterpret_cast<unsigned char*>(base);
+    const size_t s_starts = round256(sizeof(int32_t) * (size_t)(in_features + 1));
+    const size_t s_recs = round256(sizeof(int2) * (size_t)(2 * n_out * K));
+    const size_t s_cursor = round256(sizeof(int32_t) * (size_t)in_features);
+    p.starts = reinterpret_cast<int32_t*>(b);
+    p.tmp = reinterpret_cast<int2*>(b + s_starts);
+    p.recs = reinterpret_cast<int2*>(b + s_starts + s_recs);
+    p.cursor = reinterpret_cast<int32_t*>(b + s_starts + 2 * s_recs);
+    p.bytes = s_starts + 2 * s_recs + s_cursor;
+    return p;
+}
+
+__device__ __forceinline__ bool uses_a(const GatePoly& g) { return g.c1 != 0.f || g.c3 != 0.f; }
+__device__ __forceinline__ bool uses_b(const GatePoly& g) { return g.c2 != 0.f || g.c3 != 0.f; }
+
+// The occurrences of slot (j, k): up to two records, each with its destination row.
+__device__ __forceinline__ int slot_occurrences(const int2* slots, const uint8_t* gates, int64_t j, int K, int64_t k,
+                                                int64_t group, int64_t in_features, int (&row)[2], int2 (&rec)[2]) {
+    const int64_t slot = j * K + k;
+    const int g = gates[(j / group) * K + k] & 15;
+    const GatePoly gp = gate_poly(g);
+    const int2 s = slots[slot];
+    const bool ha = uses_a(gp) && s.x >= 0, hb = uses_b(gp) && s.y >= 0;
+    const int oa = uses_b(gp) ? s.y : -1, ob = uses_a(gp) ? s.x : -1;  // the other operand, if it is used
+    const int base = (int)(slot << 7) | g;
+    int n = 0;
+    if (ha) {
+        row[n] = s.x;
+        rec[n++] = make_int2(oa, base | (1 << 5));
+    }
+    if (hb) {
+        row[n] = s.y;
+        rec[n++] = make_int2(ob, base | (ha ? 0 : 1 << 5) | (1 << 4));
+    }
+    if (n == 0) {
+        row[n] = (int)(j % in_features);
+        rec[n++] = make_int2(-1, base | (1 << 6) | (1 << 5));
+    }
+    return n;
+}
+
+__global__ void index_count_kernel(const int2* slots, const uint8_t* gates, int64_t n_out, int K, int64_t group,
+                                   int64_t in_features, int32_t* counts) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n_out * K) return;
+    int row[2];
+    int2 rec[2];
+    const int n = slot_occurrences(slots, gates, e / K, K, e % K, group, in_features, row, rec);
+    for (int i = 0; i < n; ++i) atomicAdd(counts + row[i], 1);
+}
+
+// Exclusive scan of counts[0, n) into starts[0, n], one CTA.
+__global__ void __launch_bounds__(1024) index_scan_kernel(const int32_t* counts, int64_t n, int32_t* starts,
+                                                          int32_t* cursor) {
+    __shared__ int32_t part[1024];
+    const int t = threadIdx.x;
+    const int64_t per = (n + 1023) / 1024;
+    const int64_t lo = t * per < n ? t * per : n, hi = lo + per < n ? lo + per : n;
+    int32_t s = 0;
+    for (int64_t i = lo; i < hi; ++i) s += counts[i];
+    part[t] = s;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+        const int32_t v = t >= o ? part[t - o] : 0;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    int32_t run = part[t] - s;
+    for (int64_t i = lo; i < hi; ++i) {
+        const int32_t c = counts[i];  // counts may alias cursor
+        starts[i] = run;
+        cursor[i] = run;
+        run += c;
+    }
+    if (t == 1023) starts[n] = part[1023];
+}
+
+__global__ void index_fill_kernel(const int2* slots, const uint8_t* gates, int64_t n_out, int K, int64_t group,
+                                  int64_t in_features, int32_t* cursor, int2* tmp) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n_out * K) return;
+    int row[2];
+    int2 rec[2];
+    const int n = slot_occurrences(slots, gates, e / K, K, e % K, group, in_features, row, rec);
+    for (int i = 0; i < n; ++i) tmp[atomicAdd(cursor + row[i], 1)] = rec[i];
+}
+
+// Order each row's occurrences by record key (unique per slot and side): rank sort, one warp per row.
+__global__ void index_sort_kernel(const int32_t* starts, int64_t in_features, const int2* tmp, int2* recs) {
+    const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= in_features) return;
+    const int beg = starts[row], end = starts[row + 1];
+    for (int e = beg + lane; e < end; e += 32) {
+        const int2 r = tmp[e];
+        const uint32_t key = (uint32_t)r.y;
+        int rank = 0;
+        for (int q = beg; q < end; ++q) rank += (uint32_t)tmp[q].y < key;
+        recs[beg + rank] = r;
+    }
+}
+
+__device__ __forceinline__ float exp_acc(float v) { return expf(v); }
+__device__ __forceinline__ double exp_acc(double v) { return exp(v); }
+
+// Per-step probabilities p[r, k]: softmax of the logits (compactlogic.py:108), or the probabilities as given.
+template <typename A>
+__global__ void softmax_rows_kernel(const A* w, int64_t rows, int K, int mode, A* probs) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const A* wr = w + r * K;
+    A* pr = probs + r * K;
+    if (mode != CLB_W_LOGITS) {
+        for (int k = 0; k < K; ++k) pr[k] = wr[k];
+        return;
+    }
+    A m = wr[0];
+    for (int k = 1; k < K; ++k) m = wr[k] > m ? wr[k] : m;
+    A s = 0;
+    for (int k = 0; k < K; ++k) s += exp_acc(wr[k] - m);
+    for (int k = 0; k < K; ++k) pr[k] = exp_acc(wr[k] - m) / s;
+}
+
+// Butterfly reduce-scatter of N per-lane values: afterwards lane l holds the warp sum of value
+// (l >> (5 - log2 N)) & (N - 1).
+template <typename A, int N, int OFF> struct RS {
+    static __device__ __forceinline__ void run(A* v, int lane) {
+        const bool up = (lane & OFF) != 0;
+#pragma unroll
+        for (int i = 0; i < N / 2; ++i) {
+            const A send = up ? v[i] : v[i + N / 2];
+            const A keep = up ? v[i + N / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+        }
+        RS<A, N / 2, OFF / 2>::run(v, lane);
+    }
+};
+template <typename A, int OFF> struct RS<A, 1, OFF> {
+    static __device__ __forceinline__ void run(A* v, int lane) {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], OFF);
+        RS<A, 1, OFF / 2>::run(v, lane);
+    }
+};
+template <typename A> struct RS<A, 1, 0> {
+    static __device__ __forceinline__ void run(A*, int) {}
+};
+
+struct GatherArgs {
+    const void* x;
+    int64_t ldx;
+    int64_t ncols;
+    const void* gy;   // arithmetic type [n_out, ldgy], or null with the fused GroupSum
+    int64_t ldgy;
+    const void* gs_grad;
+    int64_t gs_size;
+    int64_t ld_gs;
+    double gs_scale;
+    void* gx;         // arithmetic type [in, ldgx], written
+    int64_t ldgx;
+    void* part;       // arithmetic type [nchunks, n_out, K] or null
+    const void* probs;
+    const int32_t* starts;
+    const int2* recs;
+    int64_t in_features;
+    int64_t n_out;
+    int K;
+    int64_t group;
+};
+
+// Gate coefficients of one occurrence, from the point of view of its own operand ("s", the row the
+// warp owns) and the other operand ("o"): f = c0 + cs s + co o + c3 s o.  Indexed by
+// gate | side << 4 | zero << 5 | absent << 6 (absent: the other operand is not read, the warp reads its
+// own row in its place).  zero clears cs and c3 (the own operand reads as 0 and receives no gradient);
+// absent clears co and c3 (the other operand is 0 or ignored).
+template <typename A> struct Coef { A c0, cs, co, c3; };
+
+__device__ __forceinline__ int occ_code(int meta, bool absent) { return (meta & 15) | ((meta >> 4 & 1) << 4) | ((meta >> 6 & 1) << 5) | (absent ? 64 : 0); }
+
+// One warp per (input row, column chunk); U occurrences in flight per step.  I is the index type of
+// element offsets (int when every operand fits 2^31 elements).
+template <typename T, int VEC, int U, typename I>
+__global__ void __launch_bounds__(kThreads, U == 4 ? 3 : 1) logic_backward_gather_kernel(const GatherArgs a) {
+    using Ac = typename Acc<T>::type;
+    __shared__ Coef<Ac> tab[128];
+    if (threadIdx.x < 128) {
+        const int c = threadIdx.x;
+        const GatePoly gp = gate_poly(c & 15);
+        const bool side_b = c >> 4 & 1, zero = c >> 5 & 1, absent = c >> 6 & 1;
+        Coef<Ac> e;
+        e.c0 = (Ac)gp.c0;
+        e.cs = zero ? (Ac)0 : (Ac)(side_b ? gp.c2 : gp.c1);
+        e.co = absent ? (Ac)0 : (Ac)(side_b ? gp.c1 : gp.c2);
+        e.c3 = (zero || absent) ? (Ac)0 : (Ac)gp.c3;
+        tab[c] = e;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const I row = (I)((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5));
+    if (row >= (I)a.in_features) return;
+    const int chunk = blockIdx.y;
+    const I col = (I)chunk * (32 * VEC) + lane * VEC;
+    const bool active = col < (I)a.ncols;
+    const I lcol = active ? col : 0;  // inactive lanes read column 0 with a zero weight
+    const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
+    const bool use_gs = a.gs_grad != nullptr;
+    const Ac* __restrict__ gsrc = reinterpret_cast<const Ac*>(use_gs ? a.gs_grad : a.gy);
+    const I ldg = (I)(use_gs ? a.ld_gs : a.ldgy), ldx = (I)a.ldx;
+    const Ac* __restrict__ probs = reinterpret_cast<const Ac*>(a.probs);
+    // grad_y scale (the fused GroupSum's): 0 on inactive lanes, whose column-0 reads then contribute
+    // nothing (a non-finite value there is also read by lane 0 itself)
+    const Ac gscale = active ? (Ac)(use_gs ? a.gs_scale : 1.0) : (Ac)0;
+    const int K = a.K, group = (int)a.group, gs_size = (int)a.gs_size;
+
+    Ac xi[VEC], acc[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) xi[i] = acc[i] = 0;
+    if (active) load_acc<T, VEC>(x + row * ldx + col, xi);
+
+    const int beg = a.starts[row], end = a.starts[row + 1];
+    for (int base = beg; base < end; base += 32) {
+        const int n = end - base < 32 ? end - base : 32;
+        // per-lane decode of one record: other row (own row when absent), grad_y row, p, table code
+        int lo = (int)row, lg = 0, lcode = 0, lmeta = 0;
+        Ac lp = 0;
+        if (lane < n) {
+            const int2 rec = a.recs[base + lane];
+            lmeta = rec.y;
+            const int slot = (int)((uint32_t)rec.y >> 7);
+            const int j = slot / K;
+            lp = probs[(group == 1 ? j : j / group) * K + (slot - j * K)];
+            lg = use_gs ? j / gs_size : j;
+            lo = rec.x >= 0 ? rec.x : (int)row;
+            lcode = occ_code(rec.y, rec.x < 0) | (rec.y & (1 << 5) ? 128 : 0);
+        }
+        for (int e = 0; e < n; e += U) {
+            // phase 1: issue every gather of the U occurrences before any arithmetic
+            Ac g[U][VEC], xo[U][VEC];
+            int code[U];
+            Ac pu[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int src = (e + u) & 31;
+                const int o = __shfl_sync(0xffffffffu, lo, src);
+                const int gr = __shfl_sync(0xffffffffu, lg, src);
+                code[u] = __shfl_sync(0xffffffffu, lcode, src);
+                pu[u] = __shfl_sync(0xffffffffu, lp, src);
+                if (e + u < n) {  // warp-uniform
+                    load_acc<Ac, VEC>(gsrc + (I)gr * ldg + lcol, g[u]);
+                    load_acc<T, VEC>(x + (I)o * ldx + lcol, xo[u]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < VEC; ++i) g[u][i] = xo[u][i] = 0;
+                    code[u] = 0;  // gate 0: every coefficient zero
+                }
+            }
+            // phase 2: the arithmetic
+            Ac dot[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const Coef<Ac> c = tab[code[u] & 127];
+                const Ac pcs = pu[u] * c.cs, pc3 = pu[u] * c.c3;
+                Ac d = 0;
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) {
+                    const Ac gi = g[u][i] * gscale;
+                    const Ac f = fma(fma(c.c3, xi[i], c.co), xo[u][i], fma(c.cs, xi[i], c.c0));
+                    d = fma(gi, f, d);
+                    acc[i] = fma(fma(pc3, xo[u][i], pcs), gi, acc[i]);
+                }
+                dot[u] = (code[u] & 128) ? d : (Ac)0;
+            }
+            if (a.part != nullptr) {
+                constexpr int L = U == 8 ? 3 : U == 4 ? 2 : U == 2 ? 1 : 0;
+                RS<Ac, U, 16>::run(dot, lane);
+                const int u = (lane >> (5 - L)) & (U - 1);
+                const int meta = __shfl_sync(0xffffffffu, lmeta, (e + u) & 31);
+                if ((lane & ((1 << (5 - L)) - 1)) == 0 && e + u < n && ((meta >> 5) & 1)) {
+                    const int64_t slot = (uint32_t)meta >> 7;
+                    reinterpret_cast<Ac*>(a.part)[(int64_t)chunk * a.n_out * K + slot] = dot[0];
+                }
+            }
+        }
+    }
+    if (active) store_from_acc<Ac, VEC>(reinterpret_cast<Ac*>(a.gx) + (int64_t)row * a.ldgx + col, acc);
+}
+
+template <typename T> constexpr int gvec() { return 16 / (int)sizeof(T) > 4 ? 4 : 16 / (int)sizeof(T); }
+
+inline bool al(const void* p, int bytes) { return p == nullptr || ((uintptr_t)p % bytes) == 0; }
+
+// Vector width of the gather backward for these pointers / strides (1 if any breaks alignment).
+template <typename T>
+int gather_vec(const GatherArgs& a) {
+    using Ac = typename Acc<T>::type;
+    constexpr int V = gvec<T>();
+    const bool ok = a.ncols % V == 0 && a.ldx % V == 0 && a.ldgx % V == 0 &&
+                    (a.gy == nullptr || a.ldgy % V == 0) && (a.gs_grad == nullptr || a.ld_gs % V == 0) &&
+                    al(a.x, (int)(sizeof(T) * V)) && al(a.gx, (int)(sizeof(Ac) * V > 16 ? 16 : sizeof(Ac) * V)) &&
+                    al(a.gy, (int)(sizeof(Ac) * V > 16 ? 16 : sizeof(Ac) * V)) &&
+                    al(a.gs_grad, (int)(sizeof(Ac) * V > 16 ? 16 : sizeof(Ac) * V));
+    return ok ? V : 1;
+}
+
+// Occurrences in flight per warp step.  With the column chunk's x and grad_y slabs resident in L2, 4
+// (3 CTAs per SM) issues fewer instructions per byte; when they spill to HBM, 2 (4 CTAs per SM, more
+// warps to cover DRAM latency) measured faster.  CLB_GATHER_U overrides.
+int gather_unroll(size_t slab_bytes) {
+    static const int forced = [] {
+        const char* e = getenv("CLB_GATHER_U");
+        const int v = e ? atoi(e) : 0;
+        return (v == 2 || v == 4 || v == 8) ? v : 0;
+    }();
+    if (forced) return forced;
+    return slab_bytes > (size_t(96) << 20) ? 2 : 4;
+}
+
+template <typename T, int VEC, typename I>
+cudaError_t gather_launch_vi(const GatherArgs& a, dim3 grid, cudaStream_t s) {
+    using Ac = typename Acc<T>::type;
+    const size_t slab = (size_t)(32 * VEC) * ((size_t)a.in_features * sizeof(T) + (size_t)a.n_out * sizeof(Ac));
+    switch (gather_unroll(slab)) {
+        case 2: logic_backward_gather_kernel<T, VEC, 2, I><<<grid, kThreads, 0, s>>>(a); break;
+        case 8: logic_backward_gather_kernel<T, VEC, 8, I><<<grid, kThreads, 0, s>>>(a); break;
+        default: logic_backward_gather_kernel<T, VEC, 4, I><<<grid, kThreads, 0, s>>>(a); break;
+    }
+    return cudaGetLastError();
+}
+
+template <typename T, int VEC>
+cudaError_t gather_launch_v(const GatherArgs& a, cudaStream_t s) {
+    dim3 grid((unsigned)ceil_div64(a.in_features, kWarps), (unsigned)ceil_div64(a.ncols, 32 * VEC));
+    if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+    const int64_t lim = int64_t(1) << 31;
+    const int64_t gext = a.gs_grad ? (a.n_out / a.gs_size + 1) * a.ld_gs : a.n_out * a.ldgy;
+    const bool small = a.in_features * a.ldx < lim && gext < lim && a.in_features < lim;
+    return small ? gather_launch_vi<T, VEC, int>(a, grid, s) : gather_launch_vi<T, VEC, int64_t>(a, grid, s);
+}
+
+template <typename T>
+int64_t gather_chunks_t(const GatherArgs& a) {
+    return ceil_div64(a.ncols, 32 * gather_vec<T>(a));
+}
+
+template <typename T>
+cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStream_t s) {
+    using Ac = typename Acc<T>::type;
+    const int64_t rows = a.n_out / a.group;
+    if (rows > 0) {
+        softmax_rows_kernel<Ac><<<(unsigned)ceil_div64(rows, 256), 256, 0, s>>>(
+            reinterpret_cast<const Ac*>(weights), rows, a.K, mode, reinterpret_cast<Ac*>(const_cast<void*>(a.probs)));
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (gather_vec<T>(a) == gvec<T>()) return gather_launch_v<T, gvec<T>()>(a, s);
+    return gather_launch_v<T, 1>(a, s);
+}
+
+GatherArgs make_args(const void* x, int64_t ldx, int64_t ncols, const void* gy, int64_t ldgy, const void* gs_grad,
+                     int64_t gs_size, int64_t ld_gs, double gs_scale, void* gx, int64_t ldgx, void* part,
+                     const void* probs, const IndexParts& ip, int64_t in_features, int64_t n_out, int K,
+                     int64_t group) {
+    GatherArgs a{};
+    a.x = x;
+    a.ldx = ldx;
+    a.ncols = ncols;
+    a.gy = gs_grad ? nullptr : gy;
+    a.ldgy = ldgy;
+    a.gs_grad = gs_grad;
+    a.gs_size = gs_size;
+    a.ld_gs = ld_gs;
+    a.gs_scale = gs_scale;
+    a.gx = gx;
+    a.ldgx = ldgx;
+    a.part = part;
+    a.probs = probs;
+    a.starts = ip.starts;
+    a.recs = ip.recs;
+    a.in_features = in_features;
+    a.n_out = n_out;
+    a.K = K;
+    a.group = group;
+    return a;
+}
+
+int64_t chunks_for(int dtype, const GatherArgs& a) {
+    switch (dtype) {
+        case CLB_F32: return gather_chunks_t<float>(a);
+        case CLB_F64: return gather_chunks_t<double>(a);
+        case CLB_BF16: return gather_chunks_t<__nv_bfloat16>(a);
+        case CLB_F16: return gather_chunks_t<__half>(a);
+    }
+    return -1;
+}
+
+bool dtype_ok(int d) { return d == CLB_F32 || d == CLB_F64 || d == CLB_BF16 || d == CLB_F16; }
+
+int cuda_fail(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return CLB_OK;
+    return set_error(CLB_ERR_CUDA, what);
+}
+
+}  // namespace
+
+}  // namespace clb
+
+using namespace clb;
+
+extern "C" int64_t clb_logic_index_bytes(int64_t n_out, int64_t K, int64_t in_features) {
+    if (n_out < 0 || K < 1 || in_features < 1 || n_out * K > kMaxSlots) return -1;
+    return (int64_t)index_parts(nullptr, n_out, K, in_features).bytes;
+}
+
+extern "C" int clb_logic_index_build(const int32_t* slots, int64_t n_out, int64_t K, int64_t group,
+                                     const uint8_t* gates, int64_t in_features, void* index, int64_t index_bytes,
+                                     clb_stream_t stream) {
+    const int64_t need = clb_logic_index_bytes(n_out, K, in_features);
+    if (need < 0)
+        return set_error(CLB_ERR_INVALID, "index_build: need 1 <= K, 1 <= in_features, n_out*K <= 2^24");
+    if (group < 1 || n_out % group) return set_error(CLB_ERR_INVALID, "index_build: n_out not a multiple of group");
+    if (index_bytes < need) return set_error(CLB_ERR_WORKSPACE, "index_build: index buffer too small");
+    if (!index || (n_out > 0 && (!slots || !gates))) return set_error(CLB_ERR_INVALID, "index_build: null pointer");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const IndexParts ip = index_parts(index, n_out, K, in_features);
+    // counts live in the starts array's first in_features entries until the scan rewrites them
+    cudaError_t e = cudaMemsetAsync(ip.cursor, 0, sizeof(int32_t) * (size_t)in_features, s);
+    if (e != cudaSuccess) return cuda_fail(e, "index_build: memset");
+    const int64_t slots_n = n_out * K;
+    const unsigned nb = (unsigned)ceil_div64(slots_n, 256);
+    const int2* sl = reinterpret_cast<const int2*>(slots);
+    if (nb) index_count_kernel<<<nb, 256, 0, s>>>(sl, gates, n_out, (int)K, group, in_features, ip.cursor);
+    // scan counts (in cursor) into starts; the scan also resets cursor to the row starts
+    index_scan_kernel<<<1, 1024, 0, s>>>(ip.cursor, in_features, ip.starts, ip.cursor);
+    if (nb) index_fill_kernel<<<nb, 256, 0, s>>>(sl, gates, n_out, (int)K, group, in_features, ip.cursor, ip.tmp);
+    index_sort_kernel<<<(unsigned)ceil_div64(in_features, kWarps), kThreads, 0, s>>>(ip.starts, in_features, ip.tmp,
+                                                                                    ip.recs);
+    count_launches(nb ? 4 : 2);
+    return cuda_fail(cudaGetLastError(), "index_build: launch");
+}
+
+extern "C" int64_t clb_logic_backward_gather_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols,
+                                                    const void* grad_y, int64_t ldgy, const void* gs_grad,
+                                                    int64_t ld_gs, const void* grad_x, int64_t ldgx) {
+    if (!dtype_ok(dtype)) return -1;
+    IndexParts ip{};
+    const GatherArgs a = make_args(x, ldx, ncols, grad_y, ldgy, gs_grad, 1, ld_gs, 1.0, const_cast<void*>(grad_x), ldgx,
+                                   nullptr, nullptr, ip, 1, 0, 1, 1);
+    return chunks_for(dtype, a);
+}
+
+extern "C" int clb_logic_backward_gather(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
+                                         int64_t n_out, int64_t K, int64_t group, int weight_mode,
+                                         const void* weights, const void* index, const void* grad_y, int64_t ldgy,
+                                         const void* gs_grad, int64_t gs_k, int64_t gs_size, int64_t ld_gs,
+                                         double gs_scale, void* grad_x, int64_t ldgx, void* probs, void* partials,
+                                         int64_t partials_chunks, clb_stream_t stream) {
+    if (!dtype_ok(dtype)) return set_error(CLB_ERR_DTYPE, "backward_gather: dtype");
+    if (clb_logic_index_bytes(n_out, K, in_features) < 0 || group < 1 || n_out % group)
+        return set_error(CLB_ERR_INVALID, "backward_gather: bad layer sizes");
+    if (weight_mode != CLB_W_LOGITS && weight_mode != CLB_W_PROBS)
+        return set_error(CLB_ERR_INVALID, "backward_gather: weight mode must be logits or probabilities");
+    if (ncols < 0 || ldx < ncols || ldgx < ncols) return set_error(CLB_ERR_INVALID, "backward_gather: ld < ncols");
+    if (ncols == 0 || in_features == 0) return CLB_OK;  // nothing to write (an empty grad_x may have no address)
+    if (!grad_x || !index || !probs || !weights || !x)
+        return set_error(CLB_ERR_INVALID, "backward_gather: null pointer");
+    if (gs_grad) {
+        if (gs_k < 1 || gs_size < 1 || ld_gs < ncols || gs_k * gs_size < n_out)
+            return set_error(CLB_ERR_INVALID, "backward_gather: bad GroupSum geometry");
+    } else if (n_out > 0 && (!grad_y || ldgy < ncols)) {
+        return set_error(CLB_ERR_INVALID, "backward_gather: null grad_y or ldgy < ncols");
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const IndexParts ip = index_parts(const_cast<void*>(index), n_out, K, in_features);
+    const GatherArgs a = make_args(x, ldx, ncols, grad_y, ldgy, gs_grad, gs_size, ld_gs, gs_scale, grad_x, ldgx,
+                                   partials, probs, ip, in_features, n_out, (int)K, group);
+    if (partials && chunks_for(dtype, a) != partials_chunks)
+        return set_error(CLB_ERR_INVALID, "backward_gather: partials sized for another column split");
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (dtype) {
+        case CLB_F32: e = gather_t<float>(a, weight_mode, weights, s); break;
+        case CLB_F64: e = gather_t<double>(a, weight_mode, weights, s); break;
+        case CLB_BF16: e = gather_t<__nv_bfloat16>(a, weight_mode, weights, s); break;
+        case CLB_F16: e = gather_t<__half>(a, weight_mode, weights, s); break;
+    }
+    count_launches(2);
+    return cuda_fail(e, "backward_gather: launch");
+}

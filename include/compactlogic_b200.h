@@ -219,6 +219,39 @@ int clb_logic_backward(int dtype, const void* x, int64_t ldx, int64_t ncols, con
 int clb_logic_grad_finalize(int dtype, const void* partials, int64_t nchunks, int64_t n_out, int64_t K,
                             int64_t group, int weight_mode, const void* weights, void* grad_w, clb_stream_t stream);
 
+/* ---- gather-form backward (destination-sorted, no scatter reductions) ----
+ * The same gradients as clb_logic_backward, walked by destination: a per-layer index lists for every
+ * input feature the slot operands that read it (the role of the reference's inverse connection index,
+ * LogicLayer.refresh_backward_index, compactlogic.py:184-274, consumed by logic_layer_cuda_backward_x,
+ * difflogic_kernel.cu:140-194, here extended so the same pass also yields the d loss / d prob partials of
+ * logic_layer_cuda_backward_w, difflogic_kernel.cu:82-137).  One warp per input row and column chunk
+ * gathers, for each occurrence, the other operand and grad_y of the slot's neuron; grad_x is stored once
+ * (not accumulated, not atomically), and its summation order is fixed for a given index.
+ * Requires n_out * K <= 2^24. */
+
+/* Bytes of a layer's occurrence index (-1 if the sizes are out of range). */
+int64_t clb_logic_index_bytes(int64_t n_out, int64_t K, int64_t in_features);
+
+/* Build the occurrence index from the slot table and gate ids (rebuild whenever either changes).
+ * `index` is a caller-owned device buffer of clb_logic_index_bytes() bytes. */
+int clb_logic_index_build(const int32_t* slots, int64_t n_out, int64_t K, int64_t group, const uint8_t* gates,
+                          int64_t in_features, void* index, int64_t index_bytes, clb_stream_t stream);
+
+/* Column chunks of clb_logic_backward_gather = rows of its partials scratch [nchunks, n_out, K]. */
+int64_t clb_logic_backward_gather_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, const void* grad_y,
+                                         int64_t ldgy, const void* gs_grad, int64_t ld_gs, const void* grad_x,
+                                         int64_t ldgx);
+
+/* Fused gather-form backward.  grad_x [in_features, ldgx] (arithmetic type) is written in full;
+ * partials (optional) as for clb_logic_backward, folded by clb_logic_grad_finalize; probs is a scratch
+ * [n_out/group, K] of the arithmetic type (the per-step softmax).  grad_y / GroupSum arguments as for
+ * clb_logic_backward; weight_mode CLB_W_LOGITS or CLB_W_PROBS. */
+int clb_logic_backward_gather(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features, int64_t n_out,
+                              int64_t K, int64_t group, int weight_mode, const void* weights, const void* index,
+                              const void* grad_y, int64_t ldgy, const void* gs_grad, int64_t gs_k, int64_t gs_size,
+                              int64_t ld_gs, double gs_scale, void* grad_x, int64_t ldgx, void* probs, void* partials,
+                              int64_t partials_chunks, clb_stream_t stream);
+
 /* ---- width-sharded (neuron-parallel) training, one process per GPU ----
  * Each of n_peers ranks owns a contiguous share of a dense layer's neurons and every rank holds the
  * full input activations.  The collectives are fused into the layer kernels over NVLink peer memory:
