@@ -251,13 +251,37 @@ __device__ __forceinline__ void gather(const T* __restrict__ x, int idx, int64_t
     }
 }
 
+// Offset mode (OFF): the stage holds element offsets idx * ldx instead of row ids (-1 stays -1), so a
+// gather is one multiply-add from the lane's column pointer instead of 64-bit row * stride arithmetic.
+// Used when in_features * ldx < 2^31 (and, for the backward's scatter, ldgx == ldx).
+__device__ __forceinline__ void scale_stage(int2* ab, int n, int64_t ld) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < n; e += blockDim.x) {
+        int2 v = ab[e];
+        // unused compacted entries hold stale values: unsigned arithmetic keeps their scaling defined
+        v.x = v.x >= 0 ? (int)((unsigned)v.x * (unsigned)ld) : -1;
+        v.y = v.y >= 0 ? (int)((unsigned)v.y * (unsigned)ld) : -1;
+        ab[e] = v;
+    }
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void gather_off(const T* __restrict__ xc, int off, typename Acc<T>::type (&v)[VEC]) {
+    if (off >= 0) {
+        load_acc<T, VEC>(xc + off, v);
+    } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) v[i] = 0;
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Forward: y[j, n] = sum_k p[r,k] * f_{g[r,k]}(x[a_jk, n], x[b_jk, n])   (difflogic_kernel.cu:39-78)
 // Select mode (float eval, difflogic_kernel.cu:341-369): only the chosen slot, p = 1.
 // With GroupSum fused (compactlogic.py:460-465), y is never written; per-class column sums are
 // accumulated into gs.acc instead.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC, bool PEERS>
+template <typename T, int VEC, bool PEERS, bool OFF>
 __global__ void __launch_bounds__(kThreads)
 logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, const GroupSumArgs gs,
                      const bool use_gs, const int TN, const PeerArgs pa) {
@@ -267,12 +291,14 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
     Stage<A> st = carve<A>(smem, TN, K, false);
     const int64_t j0 = (int64_t)blockIdx.x * TN;
     fill_stage<A, false>(a, j0, TN, st);
+    if (OFF) scale_stage(st.ab, TN * K, a.ldx);
     __syncthreads();
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t col = (int64_t)blockIdx.y * (32 * VEC) + lane * VEC;
     const bool active = col < a.ncols;
     const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
+    const T* __restrict__ xc = x + (active ? col : 0);
 
     A gacc[VEC];
 #pragma unroll
@@ -295,8 +321,13 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
                 const int2 pr = ab[s];
                 const A4<A> c = cf[s];
                 A va[VEC], vb[VEC];
-                gather<T, VEC>(x, pr.x, a.ldx, col, va);
-                gather<T, VEC>(x, pr.y, a.ldx, col, vb);
+                if (OFF) {
+                    gather_off<T, VEC>(xc, pr.x, va);
+                    gather_off<T, VEC>(xc, pr.y, vb);
+                } else {
+                    gather<T, VEC>(x, pr.x, a.ldx, col, va);
+                    gather<T, VEC>(x, pr.y, a.ldx, col, vb);
+                }
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) {
                     const A u = fma(c.z, va[i], c.y);  // p*(c2 + c3 a)
@@ -309,7 +340,10 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
                 const int idx = ab[s].x;
                 const A c = cf[s].x;
                 A va[VEC];
-                gather<T, VEC>(x, idx, a.ldx, col, va);
+                if (OFF)
+                    gather_off<T, VEC>(xc, idx, va);
+                else
+                    gather<T, VEC>(x, idx, a.ldx, col, va);
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) acc[i] = fma(c, va[i], acc[i]);
             }
@@ -374,7 +408,7 @@ constexpr int log2c(int n) { return n <= 1 ? 0 : 1 + log2c(n / 2); }
 // ([nchunks, n_out, K], deterministic) and folded by the finalize kernel.
 // KT > 0: K is a compile-time constant and the K partial sums live in registers.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC, int KT, bool PEERS>
+template <typename T, int VEC, int KT, bool PEERS, bool OFF>
 __global__ void __launch_bounds__(kThreads)
 logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict__ gy, const int64_t ldgy,
                       const GroupSumArgs gs, const bool use_gs, typename Acc<T>::type* __restrict__ gx,
@@ -385,6 +419,7 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
     Stage<A> st = carve<A>(smem, TN, K, true);
     const int64_t j0 = (int64_t)blockIdx.x * TN;
     fill_stage<A, true>(a, j0, TN, st);
+    if (OFF) scale_stage(st.ab, TN * K, a.ldx);
     __syncthreads();
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -392,6 +427,8 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
     const int64_t col = chunk * (32 * VEC) + lane * VEC;
     const bool active = col < a.ncols;
     const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
+    const T* __restrict__ xc = x + (active ? col : 0);
+    A* __restrict__ gxc = gx != nullptr ? gx + (active ? col : 0) : nullptr;
     const A* gsg = reinterpret_cast<const A*>(gs.grad);
 
     for (int t = warp; t < TN; t += kWarps) {
@@ -429,8 +466,13 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
             const A4<A> c = cf[s];
             A va[VEC], vb[VEC];
             if (active) {
-                gather<T, VEC>(x, pr.x, a.ldx, col, va);
-                gather<T, VEC>(x, pr.y, a.ldx, col, vb);
+                if (OFF) {
+                    gather_off<T, VEC>(xc, pr.x, va);
+                    gather_off<T, VEC>(xc, pr.y, vb);
+                } else {
+                    gather<T, VEC>(x, pr.x, a.ldx, col, va);
+                    gather<T, VEC>(x, pr.y, a.ldx, col, vb);
+                }
             } else {
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) va[i] = vb[i] = 0;
@@ -449,8 +491,13 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
                 db[i] = dfdb * pg;
             }
             if (gx != nullptr && active) {
-                if (pr.x >= 0) red_add<VEC>(gx + (int64_t)pr.x * ldgx + col, da);
-                if (pr.y >= 0) red_add<VEC>(gx + (int64_t)pr.y * ldgx + col, db);
+                if (OFF) {
+                    if (pr.x >= 0) red_add<VEC>(gxc + pr.x, da);
+                    if (pr.y >= 0) red_add<VEC>(gxc + pr.y, db);
+                } else {
+                    if (pr.x >= 0) red_add<VEC>(gx + (int64_t)pr.x * ldgx + col, da);
+                    if (pr.y >= 0) red_add<VEC>(gx + (int64_t)pr.y * ldgx + col, db);
+                }
             }
             if (KT > 0) {
                 pk[KT > 0 ? s : 0] = dot;
@@ -876,6 +923,18 @@ int env_vec(const char* name) {
     const int n = v != nullptr ? atoi(v) : 4;
     return (n == 2 || n == 8) ? n : 4;
 }
+// Offset mode of the main kernels (see scale_stage): the layer's rows must be known and every element
+// offset idx * ldx must fit an int; the backward scatters with the same offsets, so ldgx must equal ldx.
+// CLB_OFF32=0 disables it.
+bool off32_ok(const LayerArgs& a, const void* gx, int64_t ldgx) {
+    static const bool enabled = [] {
+        const char* e = getenv("CLB_OFF32");
+        return !(e && e[0] == '0');
+    }();
+    return enabled && a.in_features > 0 && a.in_features * a.ldx < (int64_t(1) << 31) &&
+           (gx == nullptr || ldgx == a.ldx);
+}
+
 int fwd_vec_f32() {
     static const int v = env_vec("CLB_FWD_VEC");
     return v;
@@ -973,7 +1032,9 @@ template <typename T, int VEC>
 void fwd_launch(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs& g, bool use_gs, dim3 grid, size_t smem,
                 int TN, cudaStream_t s, const PeerArgs& pa) {
     // the peer-store epilogue is a separate instantiation so the single-GPU kernel keeps its registers
-    auto k = pa.n ? logic_forward_kernel<T, VEC, true> : logic_forward_kernel<T, VEC, false>;
+    auto k = pa.n ? logic_forward_kernel<T, VEC, true, false>
+                  : off32_ok(a, nullptr, 0) ? logic_forward_kernel<T, VEC, false, true>
+                                            : logic_forward_kernel<T, VEC, false, false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, use_gs, TN, pa);
 }
@@ -1015,7 +1076,9 @@ cudaError_t bwd_launch(const LayerArgs& a, const void* gy, int64_t ldgy, const G
                        void* gx, int64_t ldgx, void* part, dim3 grid, size_t smem, int TN, cudaStream_t s,
                        const PeerArgs& pa) {
     using A = typename Acc<T>::type;
-    auto k = pa.n ? logic_backward_kernel<T, VEC, KT, true> : logic_backward_kernel<T, VEC, KT, false>;
+    auto k = pa.n ? logic_backward_kernel<T, VEC, KT, true, false>
+                  : off32_ok(a, gx, ldgx) ? logic_backward_kernel<T, VEC, KT, false, true>
+                                          : logic_backward_kernel<T, VEC, KT, false, false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<const A*>(gy), ldgy, g, use_gs, reinterpret_cast<A*>(gx), ldgx,
                                    reinterpret_cast<A*>(part), TN, pa);
