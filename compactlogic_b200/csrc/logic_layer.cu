@@ -408,7 +408,7 @@ constexpr int log2c(int n) { return n <= 1 ? 0 : 1 + log2c(n / 2); }
 // ([nchunks, n_out, K], deterministic) and folded by the finalize kernel.
 // KT > 0: K is a compile-time constant and the K partial sums live in registers.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC, int KT, bool PEERS, bool OFF>
+template <typename T, int VEC, int KT, bool PEERS, bool OFF, bool GX>
 __global__ void __launch_bounds__(kThreads)
 logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict__ gy, const int64_t ldgy,
                       const GroupSumArgs gs, const bool use_gs, typename Acc<T>::type* __restrict__ gx,
@@ -478,10 +478,15 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
                 for (int i = 0; i < VEC; ++i) va[i] = vb[i] = 0;
             }
             A dot = 0;
-            A da[VEC], db[VEC];
-            const A pw = pp[s];
+            if (!GX) {  // no activation gradient wanted (a network's first layer): f only
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) {
+                for (int i = 0; i < VEC; ++i)
+                    dot = fma(g[i], fma(fma(c.w, va[i], c.z), vb[i], fma(c.y, va[i], c.x)), dot);
+            }
+            A da[VEC], db[VEC];
+            const A pw = GX ? pp[s] : (A)0;
+#pragma unroll
+            for (int i = 0; i < VEC && GX; ++i) {
                 const A dfdb = fma(c.w, va[i], c.z);  // c2 + c3 a
                 const A dfda = fma(c.w, vb[i], c.y);  // c1 + c3 b
                 const A f = fma(dfdb, vb[i], fma(c.y, va[i], c.x));
@@ -490,7 +495,7 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
                 da[i] = dfda * pg;
                 db[i] = dfdb * pg;
             }
-            if (gx != nullptr && active) {
+            if (GX && gx != nullptr && active) {
                 if (OFF) {
                     if (pr.x >= 0) red_add<VEC>(gxc + pr.x, da);
                     if (pr.y >= 0) red_add<VEC>(gxc + pr.y, db);
@@ -1076,9 +1081,11 @@ cudaError_t bwd_launch(const LayerArgs& a, const void* gy, int64_t ldgy, const G
                        void* gx, int64_t ldgx, void* part, dim3 grid, size_t smem, int TN, cudaStream_t s,
                        const PeerArgs& pa) {
     using A = typename Acc<T>::type;
-    auto k = pa.n ? logic_backward_kernel<T, VEC, KT, true, false>
-                  : off32_ok(a, gx, ldgx) ? logic_backward_kernel<T, VEC, KT, false, true>
-                                          : logic_backward_kernel<T, VEC, KT, false, false>;
+    // GX = false (no grad_x) only in offset mode; the other variants check gx at run time
+    auto k = pa.n ? logic_backward_kernel<T, VEC, KT, true, false, true>
+                  : !off32_ok(a, gx, ldgx) ? logic_backward_kernel<T, VEC, KT, false, false, true>
+                  : gx != nullptr          ? logic_backward_kernel<T, VEC, KT, false, true, true>
+                                           : logic_backward_kernel<T, VEC, KT, false, true, false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<const A*>(gy), ldgy, g, use_gs, reinterpret_cast<A*>(gx), ldgx,
                                    reinterpret_cast<A*>(part), TN, pa);
