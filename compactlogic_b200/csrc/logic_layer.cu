@@ -265,14 +265,15 @@ __device__ __forceinline__ void scale_stage(int2* ab, int n, int64_t ld) {
     }
 }
 
+// All-zero bytes: the gather source of an absent operand (-1), up to 64 bytes per lane, so offset-mode
+// gathers need no branch and the compiler can issue the loads of several slots back to back.
+__device__ __align__(16) unsigned char g_zero_cols[32 * 64];
+
 template <typename T, int VEC>
 __device__ __forceinline__ void gather_off(const T* __restrict__ xc, int off, typename Acc<T>::type (&v)[VEC]) {
-    if (off >= 0) {
-        load_acc<T, VEC>(xc + off, v);
-    } else {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) v[i] = 0;
-    }
+    static_assert(sizeof(T) * VEC <= 64, "zero row holds 64 bytes per lane");
+    const T* p = off >= 0 ? xc + off : reinterpret_cast<const T*>(g_zero_cols) + (threadIdx.x & 31) * VEC;
+    load_acc<T, VEC>(p, v);
 }
 
 // ---------------------------------------------------------------------------------------------
