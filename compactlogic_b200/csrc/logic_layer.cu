@@ -398,6 +398,11 @@ template <typename A> struct ReduceScatter<A, 1, 0> {
     static __device__ __forceinline__ void run(A*, int) {}
 };
 
+#ifndef CLB_BWD_GROUP
+#define CLB_BWD_GROUP 2
+#endif
+constexpr int kBwdGroup = CLB_BWD_GROUP;  // slots whose gathers the backward issues together
+
 constexpr int log2c(int n) { return n <= 1 ? 0 : 1 + log2c(n / 2); }
 
 // ---------------------------------------------------------------------------------------------
@@ -461,23 +466,39 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
         const A* pp = st.p + t * K;
         A pk[KT > 0 ? KT : 1];
 
-#pragma unroll(KT > 0 ? KT : 4)
-        for (int s = 0; s < K; ++s) {
-            const int2 pr = ab[s];
-            const A4<A> c = cf[s];
-            A va[VEC], vb[VEC];
-            if (active) {
-                if (OFF) {
-                    gather_off<T, VEC>(xc, pr.x, va);
-                    gather_off<T, VEC>(xc, pr.y, vb);
-                } else {
-                    gather<T, VEC>(x, pr.x, a.ldx, col, va);
-                    gather<T, VEC>(x, pr.y, a.ldx, col, vb);
-                }
-            } else {
+        // Offset mode with a compile-time K: the gathers of G slots are issued before their arithmetic
+        // (branch-free, inactive lanes read column 0, which lane 0 reads as well).
+        constexpr int G = (OFF && KT > 0) ? (KT < kBwdGroup ? KT : kBwdGroup) : 1;
+#pragma unroll(KT > 0 ? KT / G : 4)
+        for (int s0 = 0; s0 < K; s0 += G) {
+            int2 prs[G];
+            A vas[G][VEC], vbs[G][VEC];
 #pragma unroll
-                for (int i = 0; i < VEC; ++i) va[i] = vb[i] = 0;
+            for (int u = 0; u < G; ++u) {
+                prs[u] = ab[s0 + u];
+                if (OFF && KT > 0) {
+                    gather_off<T, VEC>(xc, prs[u].x, vas[u]);
+                    gather_off<T, VEC>(xc, prs[u].y, vbs[u]);
+                } else if (active) {
+                    if (OFF) {
+                        gather_off<T, VEC>(xc, prs[u].x, vas[u]);
+                        gather_off<T, VEC>(xc, prs[u].y, vbs[u]);
+                    } else {
+                        gather<T, VEC>(x, prs[u].x, a.ldx, col, vas[u]);
+                        gather<T, VEC>(x, prs[u].y, a.ldx, col, vbs[u]);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < VEC; ++i) vas[u][i] = vbs[u][i] = 0;
+                }
             }
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+            const int s = s0 + u;
+            const int2 pr = prs[u];
+            const A4<A> c = cf[s];
+            const A* va = vas[u];
+            const A* vb = vbs[u];
             A dot = 0;
             if (!GX) {  // no activation gradient wanted (a network's first layer): f only
 #pragma unroll
@@ -510,6 +531,7 @@ logic_backward_kernel(const LayerArgs a, const typename Acc<T>::type* __restrict
             } else if (part != nullptr) {
                 dot = warp_sum(dot);
                 if (lane == 0) part[(chunk * a.n_out + j) * K + s] = dot;
+            }
             }
         }
         if (KT > 0 && part != nullptr) {
