@@ -251,6 +251,11 @@ __device__ __forceinline__ void gather(const T* __restrict__ x, int idx, int64_t
     }
 }
 
+#ifndef CLB_FWD_GROUP
+#define CLB_FWD_GROUP 2
+#endif
+constexpr int kFwdGroup = CLB_FWD_GROUP;  // two-operand slots whose gathers the forward issues together
+
 // Offset mode (OFF): the stage holds element offsets idx * ldx instead of row ids (-1 stays -1), so a
 // gather is one multiply-add from the lane's column pointer instead of 64-bit row * stride arithmetic.
 // Used when in_features * ldx < 2^31 (and, for the backward's scatter, ldgx == ldx).
@@ -317,8 +322,30 @@ logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, co
             const int ns = st.ns[t], n1 = st.n1[t];
             const int2* ab = st.ab + t * K;
             const A4<A>* cf = st.cf + t * K;
+            int s0 = 0;
+            if (OFF && kFwdGroup > 1) {  // the gathers of kFwdGroup slots issued before their arithmetic
+                for (; s0 + kFwdGroup <= ns; s0 += kFwdGroup) {
+                    A vas[kFwdGroup][VEC], vbs[kFwdGroup][VEC];
+#pragma unroll
+                    for (int u = 0; u < kFwdGroup; ++u) {
+                        const int2 pr = ab[s0 + u];
+                        gather_off<T, VEC>(xc, pr.x, vas[u]);
+                        gather_off<T, VEC>(xc, pr.y, vbs[u]);
+                    }
+#pragma unroll
+                    for (int u = 0; u < kFwdGroup; ++u) {
+                        const A4<A> c = cf[s0 + u];
+#pragma unroll
+                        for (int i = 0; i < VEC; ++i) {
+                            const A w = fma(c.z, vas[u][i], c.y);  // p*(c2 + c3 a)
+                            acc[i] = fma(c.x, vas[u][i], acc[i]);
+                            acc[i] = fma(w, vbs[u][i], acc[i]);
+                        }
+                    }
+                }
+            }
 #pragma unroll 4
-            for (int s = 0; s < ns; ++s) {
+            for (int s = s0; s < ns; ++s) {
                 const int2 pr = ab[s];
                 const A4<A> c = cf[s];
                 A va[VEC], vb[VEC];
