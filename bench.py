@@ -34,10 +34,10 @@ sys.path.insert(0, ROOT)
 C2 = dict(in_dim=784, width=64000, layers=6, K=16, k=10, tau=10.0, batch=1024)
 
 # DRAM bytes (read + write) per launch of the dominant c2 kernel from one ncu capture
-# (profiles/logic_layer_kernels_c2.md): 2.092 GB for a 64000->64000 layer with grad_x, 0.320 GB for the
+# (profiles/logic_layer_kernels_c2.md): 2.160 GB for a 64000->64000 layer with grad_x, 0.317 GB for the
 # 784->64000 first layer; averaged over the 6 backward launches of a step.  Cold-cache (ncu flushes
 # before each pass), so an upper bound of the steady state.
-NCU_TRAFFIC = {"logic_backward_kernel": (5 * 2.092e9 + 0.320e9) / 6}
+NCU_TRAFFIC = {"logic_backward_kernel": (5 * 2.160e9 + 0.317e9) / 6}
 C4 = dict(in_dim=784, width=256000, layers=8, k=10, tau=1.0, samples=1 << 22)
 C3 = dict(batch=512, K=16, dense=128000, k=10, tau=20.0)
 C5 = dict(in_dim=3072, width=1_000_000, layers=4, K=4, k=100, tau=30.0, batch=512)
