@@ -38,3 +38,33 @@ def test_errors_are_reported_not_fatal():
     assert st == _lib.CLB_ERR_DIVISIBILITY
     st = L.clb_tensor_packbits(None, 1, 1, 12, None, None, None)
     assert st == _lib.CLB_ERR_INVALID
+
+
+def test_gather_backward_index_sizes_and_argument_checks():
+    """Occurrence-index sizing and the gather backward's argument validation (no CUDA call is made)."""
+    L = _lib.lib()
+    r256 = lambda v: (v + 255) // 256 * 256
+    n_out, K, inf = 64000, 16, 64000
+    assert L.clb_logic_index_bytes(n_out, K, inf) == r256(4 * (inf + 1)) + 2 * r256(8 * 2 * n_out * K) + r256(4 * inf)
+    assert L.clb_logic_index_bytes(1 << 20, 16, 10) > 0                  # 2^24 slots: at the limit
+    assert L.clb_logic_index_bytes((1 << 20) + 1, 16, 10) == -1          # slot id field overflow
+    assert L.clb_logic_index_bytes(10, 0, 10) == -1
+    assert L.clb_logic_index_bytes(10, 4, 0) == -1
+    st = L.clb_logic_index_build(None, 10, 4, 3, None, 8, None, 0, None)  # n_out not a multiple of group
+    assert st == _lib.CLB_ERR_INVALID and b"group" in L.clb_last_error()
+    st = L.clb_logic_index_build(None, 10, 4, 1, None, 8, None, 16, None)  # buffer too small
+    assert st == _lib.CLB_ERR_WORKSPACE
+    args = [0, None, 8, 8, 8, 10, 4, 1, 0, None, None, None, 8, None, 0, 0, 0, 1.0, None, 8, None, None, 0, None]
+    a = list(args)
+    a[0] = 9
+    assert L.clb_logic_backward_gather(*a) == _lib.CLB_ERR_DTYPE
+    a = list(args)
+    a[8] = 2  # select mode has no gradient
+    assert L.clb_logic_backward_gather(*a) == _lib.CLB_ERR_INVALID
+    assert L.clb_logic_backward_gather(*args) == _lib.CLB_ERR_INVALID  # null pointers
+    a = list(args)
+    a[3] = 0  # no columns: nothing to do
+    assert L.clb_logic_backward_gather(*a) == _lib.CLB_OK
+    # fp32: 128 columns per chunk when everything is 16-byte aligned, 32 (scalar) otherwise
+    assert L.clb_logic_backward_gather_chunks(0, 256, 1024, 1000, 512, 1024, None, 0, 1024, 1024) == 8
+    assert L.clb_logic_backward_gather_chunks(0, 256, 1023, 1000, 512, 1023, None, 0, 1024, 1024) == 32
