@@ -33,8 +33,8 @@ sys.path.insert(0, ROOT)
 
 C2 = dict(in_dim=784, width=64000, layers=6, K=16, k=10, tau=10.0, batch=1024)
 
-# DRAM bytes (read + write) per launch of the dominant c2 kernel from one ncu capture
-# (profiles/logic_layer_kernels_c2.md): 2.160 GB for a 64000->64000 layer with grad_x, 0.317 GB for the
+# DRAM bytes (read + write) per launch of the dominant c2 kernel from one ncu capture (the backward
+# kernel summary under profiles/): 2.160 GB for a 64000->64000 layer with grad_x, 0.317 GB for the
 # 784->64000 first layer; averaged over the 6 backward launches of a step.  Cold-cache (ncu flushes
 # before each pass), so an upper bound of the steady state.
 NCU_TRAFFIC = {"logic_backward_kernel": (5 * 2.160e9 + 0.317e9) / 6}
@@ -144,7 +144,9 @@ def c2_inputs(seed, batch):
 
 
 def c2_bytes_per_step(B):
-    """Compulsory HBM bytes of one step (fp32, GroupSum fused, Adam excluded); see DESIGN.md."""
+    """Compulsory HBM bytes of one step (fp32, GroupSum fused, Adam excluded): per soft layer
+    e*B*(in + out) + n_out*K*13 forward and e*B*(2 in + out) + n_out*K*13 backward, without y for the
+    fused last layer, without grad_x for the first."""
     e, K, W, I = 4, C2["K"], C2["width"], C2["in_dim"]
     par = W * K * 13
     fwd = e * B * (I + W) + par + (C2["layers"] - 2) * (e * B * 2 * W + par) + (e * B * W + par)
