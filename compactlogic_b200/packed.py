@@ -7,8 +7,9 @@ network runs on bits: 64 samples per uint64 word, one gate evaluation per word, 
 layer is fused with a per-class vertical popcount, producing the exact integer class counts.
 
 Samples are processed in chunks of ``chunk_words`` words (64 samples each): all layers of one chunk
-run back to back so the chunk's intermediate activations (n_out x chunk_words x 8 bytes per layer)
-stay in the 126 MB L2 instead of round-tripping through HBM.
+run back to back.  At the default 128 words a 256000-wide layer's chunk activations (262 MB) exceed
+the 126 MB L2, so each layer's output streams through HBM once and is read back by the next layer;
+measured on a B200, this beats smaller L2-resident chunks, whose per-launch fixed costs dominate.
 """
 import math
 from typing import List, Optional

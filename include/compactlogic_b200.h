@@ -3,9 +3,10 @@
  *
  * Conventions
  *   - Every pointer argument is a device pointer unless its name ends in `_host`.
- *   - Every buffer is allocated by the caller.  No entry point allocates device memory; entry points
- *     that need temporary device memory take a caller-provided `workspace` and have a matching
- *     `*_workspace_bytes` query.
+ *   - Every buffer is allocated by the caller.  No compute entry point allocates device memory;
+ *     entry points that need temporary device memory take a caller-provided `workspace` and have a
+ *     matching `*_workspace_bytes` query.  The one exception is clb_peer_alloc (width-sharded
+ *     training), whose job is to cudaMalloc a buffer that other processes map over CUDA IPC.
  *   - `stream` is a cudaStream_t (pass the caller's current stream; 0 = legacy default stream).
  *     All work is enqueued asynchronously on it.  Entry points marked (sync) read a device flag
  *     back and so synchronise with the stream.
@@ -80,15 +81,20 @@ int clb_difflogic_backward_w(int dtype, const void* x, int64_t in_dim, int64_t b
                              const int64_t* b, const uint8_t* gate_seq, const void* grad_y, int64_t out_dim,
                              int64_t K, void* grad_w, void* workspace, size_t workspace_bytes, clb_stream_t stream);
 
-/* No counterpart in the reference.  Same result as clb_difflogic_backward_w, for callers that cannot
- * allocate device memory (no allocator of their own to provide a workspace, or an allocator that
- * forbids cudaMalloc where the call is made): instead of a workspace it uses an 8 MiB scratch array
- * compiled into the library, held on every GPU that loads it until exit.  Limit:
- * out_dim*K*8 + ceil(batch/(32*v))*out_dim*K*elem bytes (v = 4 for fp32, 2 for fp64 when the
- * pointers and batch allow 16-byte vectors, else 1), each part rounded up to 256, must fit in 8 MiB;
- * larger calls return CLB_ERR_WORKSPACE.  The first call on a device (with it current) looks up the
- * array's address; make it before any stream capture.  Calls share the array: calls that overlap on
- * the GPU race and must be serialised by the caller.  Allocates nothing. */
+/* No counterpart in the reference.  Same result as clb_difflogic_backward_w for fp32 and fp64 (fp16
+ * returns CLB_ERR_DTYPE: its fp32 staging copies would not fit the fixed scratch), for callers that
+ * cannot allocate device memory (no allocator of their own to provide a workspace, or an allocator
+ * that forbids cudaMalloc where the call is made): instead of a workspace it uses an 8 MiB scratch
+ * array compiled into the library, held on every GPU that loads it until exit.  Limit:
+ *   round256(out_dim*K*8) + round256(chunks*out_dim*K*elem) <= 8 MiB,
+ * chunks = clb_logic_backward_chunks(dtype, x, batch, batch, in_dim, grad_y, batch, NULL, 0, NULL, batch)
+ * (the column split depends on the pointers' alignment and the tuning environment, so query it
+ * rather than assume 128 columns per chunk), elem = 4 (fp32) or 8 (fp64); larger calls return
+ * CLB_ERR_WORKSPACE.  The first call on a device (with it current) looks up the array's address
+ * and caches it for the process's current context on that device (after cudaDeviceReset the cached
+ * address is stale: do not call this entry point again in that process); make that first call
+ * before any stream capture.  Calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing. */
 int clb_difflogic_backward_w_noalloc(int dtype, const void* x, int64_t in_dim, int64_t batch, const int64_t* a,
                                      const int64_t* b, const uint8_t* gate_seq, const void* grad_y, int64_t out_dim,
                                      int64_t K, void* grad_w, clb_stream_t stream);

@@ -41,9 +41,10 @@ def build(ref_root: str) -> None:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("COMPACTLOGIC_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("COMPACTLOGIC_REF"),
+                    help="reference checkout (default: $COMPACTLOGIC_REF)")
     args = ap.parse_args()
-    if not os.path.isdir(os.path.join(args.ref, "compactlogic", "cuda")):
+    if not args.ref or not os.path.isdir(os.path.join(args.ref, "compactlogic", "cuda")):
         print("[build_ref] reference tree not present; nothing to build")
         sys.exit(0)
     os.makedirs(OUT, exist_ok=True)

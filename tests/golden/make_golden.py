@@ -1,6 +1,6 @@
 """Generate the CPU golden fixtures of tests/golden/ from the reference CompactLogic Python code.
 
-Run in a container that has the reference tree (default /root/reference); nothing here runs at test
+Run where the reference tree is checked out (--ref or $COMPACTLOGIC_REF); nothing here runs at test
 time.  The reference package imports its CUDA extensions at module level, so they are replaced by
 empty placeholder modules (no kernel is called: only host-side code runs), and the class-definition
 default arguments that build tensors on 'cuda' are redirected to the CPU during the import.
@@ -21,7 +21,7 @@ Fixtures written (all small, npz):
                       pass-through / inverter gates with repeated operands: kept gates (node id, gate id,
                       operand signal ids) and every class-group source (constant, signal, inversion).
 
-Usage: python tests/golden/make_golden.py [--ref /root/reference]
+Usage: python tests/golden/make_golden.py --ref <reference checkout>
 """
 import argparse
 import hashlib
@@ -265,8 +265,10 @@ def freezer_trace(cl):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("COMPACTLOGIC_REF"))
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set COMPACTLOGIC_REF to the reference checkout")
     cl = import_reference(args.ref)
     gate_kat(args.ref)
     layer_buffers(cl)
