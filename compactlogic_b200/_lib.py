@@ -53,6 +53,13 @@ _SIGS = {
     "clb_logic_backward": (_int, [_int, _p, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _int, _p, _i64, _p, _i64,
                                   _i64, _i64, _dbl, _p, _i64, _int, _i64, _p, _i64, _p]),
     "clb_logic_grad_finalize": (_int, [_int, _p, _i64, _i64, _i64, _i64, _int, _p, _p, _p]),
+    "clb_conv_plane_parts": (_i64, [_i64, _i64, _int, _int, _i64]),
+    "clb_conv_plane_forward": (_int, [_int, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int,
+                                      _i64, _p, _p, _p, _p, _i64, _int, _p, _p, _p, _p, _i64, _p, _p]),
+    "clb_conv_plane_backward": (_int, [_int, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int,
+                                       _i64, _p, _p, _p, _p, _i64, _int, _p, _p, _p, _i64, _p, _i64, _int, _p, _i64,
+                                       _p, _p]),
+    "clb_l2_probe": (_int, [_int, _p, _p, _i64, _int, _int, _p, _p]),
     "clb_logic_index_bytes": (_i64, [_i64, _i64, _i64]),
     "clb_logic_index_build": (_int, [_p, _i64, _i64, _i64, _p, _i64, _p, _i64, _p]),
     "clb_logic_backward_gather_chunks": (_i64, [_int, _p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64]),

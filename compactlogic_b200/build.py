@@ -15,7 +15,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OUT_DIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(OUT_DIR, "libcompactlogic_b200.so")
-SOURCES = ["logic_layer.cu", "packed.cu", "capi.cu", "noalloc.cu", "hooks.cu", "gather_backward.cu"]
+SOURCES = ["logic_layer.cu", "packed.cu", "capi.cu", "noalloc.cu", "hooks.cu", "gather_backward.cu", "conv_plane.cu", "probe.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC,-O3",
          "-Xptxas", "-O3"]

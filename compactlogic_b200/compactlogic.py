@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
-from .functional import GradSlot, LayerSpec, LogicGroupSumFn, LogicLayerFn, eval_forward, eval_group_sum
+from .functional import ConvPlan, GradSlot, LayerSpec, LogicGroupSumFn, LogicLayerFn, eval_forward, eval_group_sum
 
 __all__ = [
     "LogicLayer", "GroupSum", "LogicLayerCudaFunction", "ConvLayer", "ConvLayerCudaFunction",
@@ -491,7 +491,26 @@ class ConvLayer(LogicLayer):
         if int(err.item()):
             raise RuntimeError(f"ConvLayer: channel offset outside [0, {c_in})")
         return LayerSpec(slots, self.gate_sequence.contiguous(), n_out, K, self.h_out * self.w_out,
-                         int(np.prod(self.in_shape)), True)
+                         int(np.prod(self.in_shape)), True, conv=self._plane_plan(och, oh, ow, device))
+
+    def _plane_plan(self, och, oh, ow, device):
+        """Channel grouping for the receptive-field-staged kernels, or None when a slot reads another
+        channel than its row's first one, or an offset lies outside [-pad, ks-1-pad]."""
+        c_in, h, w = (int(v) for v in self.in_shape)
+        lo, hi = -self.padding, self.ks - 1 - self.padding
+        chan = och[0, :, 0]
+        single = bool(((och == chan.view(1, -1, 1)).all()).item())
+        in_range = bool((((oh >= lo) & (oh <= hi)).all() & ((ow >= lo) & (ow <= hi)).all()).item())
+        if not (single and in_range):
+            return None
+        chan64 = chan.to(torch.int64)
+        order = torch.argsort(chan64, stable=True).to(torch.int32)
+        counts = torch.bincount(chan64, minlength=c_in)
+        starts = torch.zeros(c_in + 1, dtype=torch.int32, device=device)
+        starts[1:] = counts.cumsum(0).to(torch.int32)
+        return ConvPlan(c_in, h, w, int(self.c_out), int(self.h_out), int(self.w_out), int(self.stride),
+                        int(self.padding), int(self.ks), oh, ow, order, starts, int(counts.max().item()),
+                        torch.zeros(1, dtype=torch.int32, device=device))
 
     def get_connections(self, device='cuda'):
         """Sample channel and spatial offsets of every slot (compactlogic.py:642-698).

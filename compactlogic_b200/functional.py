@@ -27,6 +27,42 @@ class LayerSpec:
     # occurrence index of the gather-form backward (built on first use; the spec itself is rebuilt
     # whenever the connection or gate buffers change)
     index: Optional[torch.Tensor] = field(default=None, repr=False)
+    # receptive-field-staged conv kernels (clb_conv_plane_*), when every output channel reads one input
+    # channel; None for dense layers and for conv layers with mixed channels
+    conv: Optional["ConvPlan"] = field(default=None, repr=False)
+
+
+@dataclass
+class ConvPlan:
+    """Geometry and channel grouping of a conv layer for the receptive-field-staged kernels."""
+    c_in: int
+    h_in: int
+    w_in: int
+    c_out: int
+    h_out: int
+    w_out: int
+    stride: int
+    pad: int
+    ks: int
+    off_h: torch.Tensor   # int8 [2, c_out, K] (the layer's offsets_h buffer)
+    off_w: torch.Tensor
+    order: torch.Tensor   # int32 [c_out]: output channels grouped by input channel
+    starts: torch.Tensor  # int32 [c_in + 1]
+    max_group: int
+    err: torch.Tensor     # int32 [1]: bit 1 set if a staging wait gave up
+
+
+def _plane_ok(spec: "LayerSpec", xt: torch.Tensor, *others) -> bool:
+    """Whether the staged conv kernels take this call: fp32, 16-byte rows, K in {4, 8, 16}."""
+    if spec.conv is None or os.environ.get("CLB_CONV_PLANE", "1") == "0" or xt.dtype != torch.float32:
+        return False
+    B = xt.shape[1]
+    for t in (xt,) + others:
+        if t is None:
+            continue
+        if t.data_ptr() % 16 or (t.dim() == 2 and t.stride(0) % 4):
+            return False
+    return B % 4 == 0 and spec.K in (4, 8, 16)
 
 
 def _gather_backward_enabled(spec: "LayerSpec") -> bool:
@@ -61,7 +97,9 @@ class KernelTimer:
       backward = e*B*in + a*B*out + a*B*in + n_out*K*8 + rows*K*5
                  (gy term dropped when synthesised from the fused GroupSum, gx term when not needed)
     with e the activation element size, a the gradient element size, slots int32 pairs, gate ids
-    uint8 and logits fp32."""
+    uint8 and logits fp32.  Each record also carries the launch's L2 gather / reduction bytes: one
+    e-byte read per used operand and column (operands a gate ignores are never touched), plus, in the
+    backward, one a-byte reduction per used operand and column when grad_x is produced."""
 
     def __init__(self):
         self.enabled = False
@@ -70,26 +108,51 @@ class KernelTimer:
     def reset(self):
         self.records = []
 
-    def launch(self, kind, nbytes, fn):
+    def launch(self, kind, nbytes, fn, l2_bytes=0):
         if not self.enabled:
             return fn()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         out = fn()
         e.record()
-        self.records.append((kind, s, e, nbytes))
+        self.records.append((kind, s, e, nbytes, l2_bytes))
         return out
 
     def summary(self):
-        """{kind: (launches, total_ms, total_bytes)} (call after a synchronize)."""
+        """{kind: (launches, total_ms, total_bytes, total_l2_bytes)} (call after a synchronize)."""
         res = {}
-        for kind, s, e, nb in self.records:
-            n, ms, b = res.get(kind, (0, 0.0, 0))
-            res[kind] = (n + 1, ms + s.elapsed_time(e), b + nb)
+        for kind, s, e, nb, l2 in self.records:
+            n, ms, b, c = res.get(kind, (0, 0.0, 0, 0))
+            res[kind] = (n + 1, ms + s.elapsed_time(e), b + nb, c + l2)
         return res
 
 
 TIMER = KernelTimer()
+
+
+_USED_A = [1 if (((g >> 1) & 1) != ((g >> 3) & 1)) or (((g >> 3) & 1) - ((g >> 2) & 1) - ((g >> 1) & 1) + (g & 1)) else 0
+           for g in range(16)]
+_USED_B = [1 if (((g >> 2) & 1) != ((g >> 3) & 1)) or (((g >> 3) & 1) - ((g >> 2) & 1) - ((g >> 1) & 1) + (g & 1)) else 0
+           for g in range(16)]
+
+
+def used_operands(spec: "LayerSpec") -> int:
+    """Operands the layer's gates read, over all n_out * K slots (gates 0 / 15 read none, 3 / 5 / 10 / 12
+    one), cached on the spec."""
+    n = getattr(spec, "_used_ops", None)
+    if n is None:
+        tab = torch.tensor([a + b for a, b in zip(_USED_A, _USED_B)], dtype=torch.int64, device=spec.gates.device)
+        n = int(tab[(spec.gates.to(torch.int64) & 15)].sum().item()) * spec.group
+        spec._used_ops = n
+    return n
+
+
+def _bwd_l2(spec: "LayerSpec", xt: torch.Tensor, need_gx: bool) -> int:
+    """L2 gather + reduction bytes of a backward launch (see KernelTimer)."""
+    if not TIMER.enabled:
+        return 0
+    a = 8 if xt.dtype == torch.float64 else 4
+    return used_operands(spec) * xt.shape[1] * (xt.element_size() + (a if need_gx else 0))
 
 
 def _param_bytes(spec: "LayerSpec") -> int:
@@ -110,12 +173,21 @@ def forward_into(xt: torch.Tensor, weights: Optional[torch.Tensor], spec: LayerS
     B = xt.shape[1]
     e = xt.element_size()
     nbytes = e * B * (spec.in_features + (spec.n_out if y is not None else 0)) + _param_bytes(spec)
+    l2 = used_operands(spec) * B * e if TIMER.enabled else 0
+    if gs_acc is None and y is not None and _plane_ok(spec, xt, y):
+        c = spec.conv
+        TIMER.launch("conv_forward" if mode != L.W_SELECT else "conv_eval", nbytes, lambda: L.call(
+            "clb_conv_plane_forward", L.CLB_F32, L.ptr(xt), xt.stride(0), B, c.c_in, c.h_in, c.w_in, c.c_out,
+            c.h_out, c.w_out, c.stride, c.pad, c.ks, spec.K, L.ptr(c.off_h), L.ptr(c.off_w), L.ptr(c.order),
+            L.ptr(c.starts), c.max_group, mode, L.ptr(weights), L.ptr(spec.gates), L.ptr(select), L.ptr(y),
+            y.stride(0), L.ptr(c.err), L.stream(xt.device)), l2)
+        return
     TIMER.launch("forward" if mode != L.W_SELECT else "eval", nbytes, lambda: L.call(
         "clb_logic_forward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, spec.in_features, L.ptr(spec.slots),
         spec.n_out,
         spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), L.ptr(select), int(spec.has_pad), L.ptr(y),
         y.stride(0) if y is not None else 0, L.ptr(gs_acc), gs_acc.shape[0] if gs_acc is not None else 0, gs_size,
-        gs_acc.stride(0) if gs_acc is not None else 0, L.stream(xt.device)))
+        gs_acc.stride(0) if gs_acc is not None else 0, L.stream(xt.device)), l2)
 
 
 def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode: int,
@@ -129,6 +201,8 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
     B = xt.shape[1]
     acc = L.acc_dtype(xt.dtype)
     dev = xt.device
+    if gs_grad is None and mode in (L.W_LOGITS, L.W_PROBS) and _plane_ok(spec, xt, gy):
+        return _backward_conv_plane(xt, weights, spec, mode, gy, need_gx, need_gw)
     gx = torch.empty(spec.in_features, B, dtype=acc, device=dev) if need_gx else None
     gy_ptr, ldgy = (L.ptr(gy), gy.stride(0)) if gy is not None else (0, 0)
     gs_ptr, ld_gs, gs_k = (L.ptr(gs_grad), gs_grad.stride(0), gs_grad.shape[0]) if gs_grad is not None else (0, 0, 0)
@@ -145,7 +219,8 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
     TIMER.launch("backward", nbytes, lambda: L.call(
         "clb_logic_backward", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, L.ptr(spec.slots), spec.n_out,
         spec.K, spec.group, mode, L.ptr(weights), L.ptr(spec.gates), int(spec.has_pad), gy_ptr, ldgy, gs_ptr, gs_k,
-        gs_size, ld_gs, float(gs_scale), L.ptr(gx), B, 1, spec.in_features, L.ptr(part), chunks, L.stream(dev)))
+        gs_size, ld_gs, float(gs_scale), L.ptr(gx), B, 1, spec.in_features, L.ptr(part), chunks, L.stream(dev)),
+        _bwd_l2(spec, xt, need_gx))
     gw = None
     if need_gw:
         gw = torch.empty(spec.n_out // spec.group, spec.K, dtype=acc, device=dev)
@@ -153,6 +228,31 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
                      lambda: L.call("clb_logic_grad_finalize", L.dtype_code(xt.dtype), L.ptr(part),
                                     chunks if B > 0 else 0, spec.n_out, spec.K, spec.group, mode, L.ptr(weights),
                                     L.ptr(gw), L.stream(dev)))
+    return gx, gw
+
+
+def _backward_conv_plane(xt, weights, spec, mode, gy, need_gx, need_gw):
+    """Conv layer backward on the receptive-field-staged kernel (clb_conv_plane_backward): grad_x
+    (accumulated from shared-memory tiles) and per-(tile, column chunk) partials of d loss / d p,
+    folded with the softmax backward by clb_logic_grad_finalize over the c_out parameter rows."""
+    c = spec.conv
+    B = xt.shape[1]
+    dev = xt.device
+    gx = torch.empty(spec.in_features, B, dtype=torch.float32, device=dev) if need_gx else None
+    nparts = int(L.lib().clb_conv_plane_parts(c.h_out, c.w_out, c.stride, c.ks, B))
+    part = torch.empty(max(nparts, 1), c.c_out, spec.K, dtype=torch.float32, device=dev)
+    nbytes = 4 * B * (spec.in_features + spec.n_out + (spec.in_features if need_gx else 0)) + _param_bytes(spec)
+    TIMER.launch("conv_backward", nbytes, lambda: L.call(
+        "clb_conv_plane_backward", L.CLB_F32, L.ptr(xt), xt.stride(0), B, c.c_in, c.h_in, c.w_in, c.c_out, c.h_out,
+        c.w_out, c.stride, c.pad, c.ks, spec.K, L.ptr(c.off_h), L.ptr(c.off_w), L.ptr(c.order), L.ptr(c.starts),
+        c.max_group, mode, L.ptr(weights), L.ptr(spec.gates), L.ptr(gy), gy.stride(0), L.ptr(gx), B, 1, L.ptr(part),
+        nparts, L.ptr(c.err), L.stream(dev)), _bwd_l2(spec, xt, need_gx))
+    gw = None
+    if need_gw:
+        gw = torch.empty(c.c_out, spec.K, dtype=torch.float32, device=dev)
+        TIMER.launch("finalize", (nparts + 1) * c.c_out * spec.K * 4, lambda: L.call(
+            "clb_logic_grad_finalize", L.CLB_F32, L.ptr(part), nparts if B > 0 else 0, c.c_out, spec.K, 1, mode,
+            L.ptr(weights), L.ptr(gw), L.stream(dev)))
     return gx, gw
 
 

@@ -225,6 +225,41 @@ int clb_logic_backward(int dtype, const void* x, int64_t ldx, int64_t ncols, con
 int clb_logic_grad_finalize(int dtype, const void* partials, int64_t nchunks, int64_t n_out, int64_t K,
                             int64_t group, int weight_mode, const void* weights, void* grad_w, clb_stream_t stream);
 
+/* ---- receptive-field-staged conv layers (fp32) ----
+ * Native fast path of ConvLayer (compactlogic.py:598-640 with conv_layer_cuda_forward / _backward_x /
+ * _backward_w / eval, compactlogic/cuda/convlogic_kernel.cu:86-530) for layers whose every slot reads
+ * one input channel per output channel (the default num_chn == 1 connections).  x [c_in*h_in*w_in, ldx]
+ * and y / grad_y [c_out*h_out*w_out, ld] are feature-major; off_h / off_w are the layer's int8
+ * offsets_h / offsets_w buffers [2, c_out, K] (already shifted by -pad, each in [-pad, ks-1-pad]);
+ * order [c_out] lists the output channels grouped by the input channel they read and starts
+ * [c_in+1] delimits the groups; max_group is the largest group.  ncols, ldx and every ld must be
+ * multiples of 4 and the pointers 16-byte aligned; K a power of two <= 32.  err (optional, device int32) gets bit 1 set if a
+ * staging wait gave up (the kernel then skips its tile instead of hanging). */
+int64_t clb_conv_plane_parts(int64_t h_out, int64_t w_out, int stride, int ks, int64_t ncols);
+int clb_conv_plane_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t c_in, int64_t h_in,
+                           int64_t w_in, int64_t c_out, int64_t h_out, int64_t w_out, int stride, int pad, int ks,
+                           int64_t K, const int8_t* off_h, const int8_t* off_w, const int32_t* order,
+                           const int32_t* starts, int64_t max_group, int weight_mode, const void* weights,
+                           const uint8_t* gates, const uint8_t* select, void* y, int64_t ldy, int32_t* err,
+                           clb_stream_t stream);
+/* grad_x (optional) [c_in*h_in*w_in, ldgx], zeroed first when zero_grad_x; partials
+ * [clb_conv_plane_parts(), c_out, K] of d loss / d prob, folded by clb_logic_grad_finalize with
+ * n_out = c_out and group = 1.  K must be 4, 8 or 16. */
+int clb_conv_plane_backward(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t c_in, int64_t h_in,
+                            int64_t w_in, int64_t c_out, int64_t h_out, int64_t w_out, int stride, int pad, int ks,
+                            int64_t K, const int8_t* off_h, const int8_t* off_w, const int32_t* order,
+                            const int32_t* starts, int64_t max_group, int weight_mode, const void* weights,
+                            const uint8_t* gates, const void* grad_y, int64_t ldgy, void* grad_x, int64_t ldgx,
+                            int zero_grad_x, void* partials, int64_t nparts, int32_t* err, clb_stream_t stream);
+
+/* Measurement helper, no reference counterpart: throughput probe of the soft kernels' access pattern
+ * (512-byte row gathers at hashed rows, mode 0; plus as many 512-byte red.global.add.v4.f32 row
+ * reductions, mode 1) over src / dst slabs of `rows` rows; `ctas` CTAs of 256 threads, `iters` steps
+ * per warp; sink is a device float the loads are kept live through.  The benchmark sizes the slabs
+ * like one column chunk of a layer and reports the kernels' L2 traffic against it. */
+int clb_l2_probe(int mode, const float* src, float* dst, int64_t rows, int iters, int ctas, float* sink,
+                 clb_stream_t stream);
+
 /* ---- gather-form backward (destination-sorted, no scatter reductions) ----
  * The same gradients as clb_logic_backward, walked by destination: a per-layer index lists for every
  * input feature the slot operands that read it (the role of the reference's inverse connection index,
