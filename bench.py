@@ -53,6 +53,9 @@ C5 = dict(in_dim=3072, width=1_000_000, layers=4, K=4, k=100, tau=30.0, batch=51
 #  - the c4 pass (2^22 samples, 128-word chunks = 512 chunks): per chunk one first-layer launch
 #    (~0.263 GB: its 0.8 MB input + 262 MB output), six inner-layer launches (0.583 GB each, measured)
 #    and one fused count launch (0.343 GB, measured).
+# Checksum of the gathered c4 class counts (sum over samples i and classes of count * (i % 1009 + 1)) for the
+# fixed seeds of build_c4 / c4_words, measured on one B200: every N must reproduce it.
+C4_COUNTS_CHECKSUM = 270315957402565
 NCU_TRAFFIC = {"logic_backward_kernel": (5 * 2.160e9 + 0.317e9) / 6,
                "packed_pass": 512 * (0.263e9 + 6 * 0.583e9 + 0.343e9)}
 
@@ -899,6 +902,7 @@ def bench_c4(args, dev, rank, world, chunk_words):
                      "note": "byte model: every layer's activations make one HBM round trip; traffic = per-launch "
                              "ncu DRAM bytes (profiles/packed_inference_c4.md) summed over the pass's launches"},
         "counts_checksum": checksum,
+        "counts_match_single_gpu": (checksum == C4_COUNTS_CHECKSUM) if C4["samples"] == 1 << 22 else None,
         "clocks": clk.summary(),
         "e2e": {"value": round(evals / (ms_e2e / 1e3), 1), "unit": "gate-evals/s",
                 "h2d_bytes_per_step": xh.numel() * 8, "d2h_bytes_per_step": ch.numel() * 4},
