@@ -419,6 +419,8 @@ def bench_c2(args, dev, rank, world, strong=False):
         "e2e": e2e,
         "gpu_launches": launches,
     }
+    if world == 1 and not width and full and not args.no_sub:
+        res["with_resampler"] = bench_c2_resampler(args, dev, model, params, step, x_dev, y_dev, ms)
     if world > 1 and not width:
         res["replicas_identical"] = replica_checksum(params, dev)
         if evs:
@@ -428,6 +430,32 @@ def bench_c2(args, dev, rank, world, strong=False):
                               "what": "wait for the last per-layer gradient bucket after the last backward kernel "
                                       "(the first layer's bucket has no backward work left to overlap)"}
     return res, model
+
+
+def bench_c2_resampler(args, dev, model, params, step, x_dev, y_dev, ms_plain):
+    """The c2 step followed by EntropyRowResampler.step (compactlogic.py:1113-1150) every iteration, in a
+    stress setting where every row of every layer counts as converged after 2 steps (eps 1, patience 2):
+    the device monitor, one host read per step, then per layer one resampling kernel and a device sort of
+    the inverse index.  With the reference's default patience (200) nothing would be resampled inside a
+    short timed window and only the monitor would run."""
+    import compactlogic_b200 as cl
+    opt_state = {}
+
+    class _Opt:  # the resampler only reads optimizer.state; Adam moments live in the step's optimizer
+        state = opt_state
+    rs = cl.EntropyRowResampler([m for m in model if hasattr(m, "indices")], ema_decay=0.99, eps=1.0, patience=2,
+                                threshold_high=0.95, threshold_low=0.2)
+    it = [0]
+
+    def stepr():
+        step(x_dev, y_dev)
+        rs.step(it[0], _Opt)
+        it[0] += 1
+    ms = timed(stepr, args.steps, args.warmup, dev)
+    return {"ms_per_step": round(ms, 4), "value": round(C2["batch"] / (ms / 1e3), 1), "unit": "samples/s",
+            "overhead_vs_plain": round(ms / ms_plain - 1, 4),
+            "setting": "EntropyRowResampler(eps=1, patience=2, threshold_low=0.2, threshold_high=0.95): every row "
+                       "is picked each step after the second; weak/strong rows rewritten on the device"}
 
 
 def bench_c2_reference_kernels(args, dev):

@@ -78,6 +78,8 @@ _SIGS = {
     "clb_cast": (_int, [_int, _p, _int, _p, _i64, _p]),
     "clb_pack_inputs": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "clb_entropy_monitor": (_int, [_p, _i64, _i64, ctypes.c_float, ctypes.c_float, _int, _int, _p, _p, _p, _p, _p]),
+    "clb_resample_rows": (_int, [_p, _p, _p, _p, _i64, _i64, _p, ctypes.c_float, ctypes.c_float, _int, _int, _p, _p,
+                                 _p, _p, _p, _p, _p, _p, _p]),
     "clb_pack_thresholds": (_int, [_int, _p, _i64, _i64, _i64, _int, _p, _i64, _p]),
     "clb_packed_select": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _p]),
     "clb_packed_layer": (_int, [_p, _i64, _i64, _p, _p, _i64, _p, _i64, _p]),

@@ -243,13 +243,17 @@ class LogicLayer(torch.nn.Module):
 
     @torch.no_grad()
     def resample_connections(self, converged_rows, threshold_high: float = 0.95, threshold_low: float = 0.0,
-                             update_gate=True, keep_strong_weights=True):
+                             update_gate=True, keep_strong_weights=True, draws=None):
         """Re-draw rows whose gate distribution converged (compactlogic.py:282-348).
 
         Weak rows (max prob < threshold_low): new N(0,1) logits, new random gates and connections for
         every slot.  Strong rows (max prob > threshold_high): keep the winning slot with logit
         log(p (K-1) / (1-p)) (or log(9 (K-1))), zero the others and give them new gates and
-        connections.  Returns (weak_mask, strong_mask)."""
+        connections.  Returns (weak_mask, strong_mask).
+
+        ``draws`` (optional, from ``resample_draws``): take the random values from these full-size tensors
+        at the rewritten positions instead of drawing them in the reference's order; the device path
+        (``resample_rows_device``) consumes the same tensors, so both give identical buffers."""
         dev = self.weights.device
         rows = self.weights.shape[0]
         assert len(converged_rows.shape) == 1
@@ -264,10 +268,15 @@ class LogicLayer(torch.nn.Module):
         pool = torch.arange(16, device=dev, dtype=torch.uint8)
 
         if n_weak:
-            self.weights[weak_mask] = torch.randn((n_weak, self.num_gates), device=dev)
+            self.weights[weak_mask] = (draws["logits"][weak_mask] if draws is not None else
+                                       torch.randn((n_weak, self.num_gates), device=dev))
             if update_gate:
-                self.gate_sequence[weak_mask] = pool[torch.randint(0, len(pool), (n_weak, self.num_gates), device=dev)]
-            self.update_indices_weak(n_weak, weak_mask)
+                self.gate_sequence[weak_mask] = (draws["gates"][weak_mask] if draws is not None else
+                                                 pool[torch.randint(0, len(pool), (n_weak, self.num_gates), device=dev)])
+            if draws is not None:
+                self._indices_from_draws(weak_mask, draws)
+            else:
+                self.update_indices_weak(n_weak, weak_mask)
 
         if n_strong:
             refill = torch.zeros_like(self.weights, dtype=torch.bool, device=dev)
@@ -281,12 +290,108 @@ class LogicLayer(torch.nn.Module):
                                                   else np.log(9 * (self.num_gates - 1)))
             n_fill = refill.sum().item()
             if update_gate and n_fill > 0:
-                self.gate_sequence[refill] = pool[torch.randint(0, len(pool), (n_fill,), device=dev)]
-            self.update_indices_strong(refill, n_fill)
+                self.gate_sequence[refill] = (draws["gates"][refill] if draws is not None else
+                                              pool[torch.randint(0, len(pool), (n_fill,), device=dev)])
+            if draws is not None:
+                self._indices_from_draws(refill, draws)
+            else:
+                self.update_indices_strong(refill, n_fill)
         if n_weak or n_strong:
             self.refresh_backward_index(
                 torch.nonzero(torch.logical_or(weak_mask, strong_mask), as_tuple=False).flatten())
         return weak_mask, strong_mask
+
+    def _indices_from_draws(self, mask, draws):
+        if not hasattr(self, "indices"):
+            raise NotImplementedError("resampling from pre-drawn tensors is implemented for LogicLayer connections")
+        self.indices[0][mask] = draws["a"][mask]
+        self.indices[1][mask] = draws["b"][mask]
+
+    @torch.no_grad()
+    def resample_draws(self, generator=None):
+        """Full-size random tensors for one resampling call: N(0,1) logits, gate ids in [0, 16) and the two
+        operands' inputs in [0, in_dim), each [rows, K] on the layer's device."""
+        dev = self.weights.device
+        shape = tuple(self.weights.shape)
+        return {"logits": torch.randn(shape, device=dev, generator=generator),
+                "gates": torch.randint(0, 16, shape, device=dev, dtype=torch.uint8, generator=generator),
+                "a": torch.randint(0, self.in_dim, shape, device=dev, dtype=torch.int64, generator=generator),
+                "b": torch.randint(0, self.in_dim, shape, device=dev, dtype=torch.int64, generator=generator)}
+
+    def device_resample_ok(self) -> bool:
+        """Whether ``resample_rows_device`` handles this layer: a dense CUDA layer, fp32 logits, K <= 32."""
+        return (type(self) is not ConvLayer and hasattr(self, "indices") and self.weights.is_cuda and
+                self.weights.dtype == torch.float32 and self.num_gates <= 32 and self.weights.is_contiguous())
+
+    @torch.no_grad()
+    def resample_rows_device(self, picked: torch.Tensor, draws=None, threshold_high: float = 0.95,
+                             threshold_low: float = 0.0, update_gate=True, keep_strong_weights=True,
+                             adam_state=None, counter=None) -> torch.Tensor:
+        """``resample_connections`` for the rows flagged in ``picked`` (uint8 [rows], on the device), as one
+        kernel (clb_resample_rows) plus a sort-based inverse-index rebuild: nothing is read back to the host.
+        Also zeroes the Adam moments (``adam_state``, the optimizer's state dict of ``weights``) of changed
+        rows and resets ``counter`` on picked rows.  Returns the changed-row mask (uint8 [rows])."""
+        if not self.device_resample_ok():
+            raise RuntimeError("resample_rows_device: needs a dense CUDA layer with fp32 logits and K <= 32")
+        draws = draws if draws is not None else self.resample_draws()
+        dev = self.weights.device
+        rows, K = self.weights.shape
+        changed = torch.empty(rows, dtype=torch.uint8, device=dev)
+        st = adam_state or {}
+        m1, m2 = st.get("exp_avg"), st.get("exp_avg_sq")
+        w = self.weights.data
+        L.call("clb_resample_rows", L.ptr(w), L.ptr(self.gate_sequence), L.ptr(self.indices[0]),
+               L.ptr(self.indices[1]), rows, K, L.ptr(picked), float(threshold_high), float(threshold_low),
+               int(bool(keep_strong_weights)), int(bool(update_gate)), L.ptr(draws["logits"]), L.ptr(draws["gates"]),
+               L.ptr(draws["a"]), L.ptr(draws["b"]), L.ptr(changed), L.ptr(m1), L.ptr(m2), L.ptr(counter),
+               L.stream(dev))
+        # the kernel rewrote the buffers in place: bump their versions so the slot table is rebuilt
+        self.indices.add_(0)
+        self.gate_sequence.add_(0)
+        if "max_exp_avg_sq" in st:
+            st["max_exp_avg_sq"].masked_fill_(changed.bool()[:, None], 0.0)
+        self.refresh_backward_index_device(changed)
+        return changed
+
+    @torch.no_grad()
+    def refresh_backward_index_device(self, changed: torch.Tensor = None) -> None:
+        """``refresh_backward_index`` with no host synchronisation: one sort of a 64-bit key per (neuron,
+        slot, operand) entry, (input << 32) | position, where an entry of an unchanged neuron keeps its
+        position in the current index and an entry of a changed neuron (``changed`` uint8 [out], None =
+        all) is placed after them in the order the host rebuild appends it (operand a of every changed
+        row, then operand b; rows ascending, slots ascending).  The start offsets equal the host path's and
+        every input's entries are the same set; within an input the order is the entry list's (a stable
+        sort), which the host's unstable argsort (kept for the reference's CPU order) may permute."""
+        dev = self.indices.device
+        n_out, K = self.indices.shape[1], self.indices.shape[2]
+        M = 2 * n_out * K
+        eid = torch.arange(M, device=dev, dtype=torch.int64)
+        side, rem = eid // (n_out * K), eid % (n_out * K)
+        j, k = rem // K, rem % K
+        inputs = self.indices.reshape(-1)
+        if changed is None or "given_x_indices_of_y_start" not in self._buffers:
+            key = eid
+        else:
+            ch = changed.to(torch.int64)
+            rank = torch.cumsum(ch, 0) - ch  # rank of a changed row among the changed rows
+            nc = ch.sum()
+            codes_old = self.given_x_indices_of_gate.to(torch.int64)
+            old_side = (codes_old < 0).to(torch.int64)
+            old_k = torch.where(codes_old < 0, -codes_old - 1, codes_old)
+            old_eid = old_side * (n_out * K) + self.given_x_indices_of_y * K + old_k
+            pos = torch.empty(M, dtype=torch.int64, device=dev)
+            pos.scatter_(0, old_eid, eid)
+            new_key = M + side * nc * K + rank[j] * K + k
+            key = torch.where(ch[j] > 0, new_key, pos)
+        order = torch.sort((inputs << 32) | key).indices
+        counts = torch.zeros(self.in_dim, dtype=torch.int64, device=dev)
+        counts.scatter_add_(0, inputs, torch.ones_like(inputs))
+        starts = torch.zeros(self.in_dim + 1, dtype=torch.int64, device=dev)
+        starts[1:] = torch.cumsum(counts, 0)
+        self._set_or_register_buffer("given_x_indices_of_y_start", starts)
+        self._set_or_register_buffer("given_x_indices_of_y", j[order])
+        self._set_or_register_buffer("given_x_indices_of_gate",
+                                     torch.where(side[order] > 0, -(k[order] + 1), k[order]).to(torch.int8))
 
     @torch.no_grad()
     def update_indices_weak(self, n_weak, weak_mask):
@@ -773,6 +878,11 @@ class EntropyRowResampler:
     #: on CUDA layers with fp32 logits, run the per-row monitor as one fused kernel per layer and read
     #: the converged counts of all layers with a single host synchronisation per step
     use_device_monitor = True
+    #: with the device monitor, rewrite converged rows of dense layers with one kernel per layer and rebuild
+    #: the inverse index with a device sort (no further synchronisation).  The random values come from
+    #: full-size draws (LogicLayer.resample_draws) instead of the reference's count-sized draws, so the
+    #: buffers match the reference's in distribution, not bit for bit under one seed; set False for that.
+    use_device_resample = True
 
     @torch.no_grad()
     def step(self, iter: int, optimizer):
@@ -829,7 +939,12 @@ class EntropyRowResampler:
             return
         host_counts = counts.cpu()  # the one synchronisation of the step
         for i, idx, layer, flags in pending:
-            if int(host_counts[i]) > 0:
+            if int(host_counts[i]) == 0:
+                continue
+            if self.use_device_resample and layer.device_resample_ok():
+                layer.resample_rows_device(flags, adam_state=optimizer.state.get(layer.weights, None),
+                                           counter=self.counter[idx], **self.resample_kwargs)
+            else:
                 self._resample(idx, layer, flags.nonzero(as_tuple=False).flatten(), optimizer)
 
     @torch.no_grad()

@@ -348,6 +348,21 @@ int clb_entropy_monitor(const float* logits, int64_t rows, int64_t K, float ema_
                        "entropy_monitor");
 }
 
+int clb_resample_rows(float* logits, uint8_t* gates, int64_t* idx_a, int64_t* idx_b, int64_t rows, int64_t K,
+                      const uint8_t* picked, float threshold_high, float threshold_low, int keep_strong_weights,
+                      int update_gate, const float* draw_logits, const uint8_t* draw_gates, const int64_t* draw_a,
+                      const int64_t* draw_b, uint8_t* changed, float* exp_avg, float* exp_avg_sq, int32_t* counter,
+                      clb_stream_t stream) {
+    if (rows < 0 || K < 1 || K > 32) return fail(CLB_ERR_INVALID, "resample_rows: K must be in [1, 32]");
+    if (rows > 0 && (!logits || !gates || !idx_a || !idx_b || !picked || !draw_logits || !draw_gates || !draw_a ||
+                     !draw_b || !changed))
+        return fail(CLB_ERR_INVALID, "resample_rows: null");
+    return cuda_status(launch_resample_rows(logits, gates, idx_a, idx_b, rows, (int)K, picked, threshold_high,
+                                            threshold_low, keep_strong_weights, update_gate, draw_logits, draw_gates,
+                                            draw_a, draw_b, changed, exp_avg, exp_avg_sq, counter, S(stream)),
+                       "resample_rows");
+}
+
 int clb_pack_thresholds(int dtype, const void* x, int64_t batch, int64_t features, int64_t ldx, int nthr,
                         uint64_t* out, int64_t ldw, clb_stream_t stream) {
     if (!dtype_ok(dtype)) return fail(CLB_ERR_DTYPE, "pack_thresholds: dtype");

@@ -112,6 +112,13 @@ cudaError_t launch_entropy_monitor(const float* logits, int64_t rows, int K, flo
                                    int32_t* counter, int first, float decay, float eps, int patience,
                                    uint8_t* converged, int32_t* n_converged, cudaStream_t s);
 
+// Device row resampling of LogicLayer.resample_connections from pre-drawn random tensors (hooks.cu).
+cudaError_t launch_resample_rows(float* logits, uint8_t* gates, int64_t* idx_a, int64_t* idx_b, int64_t rows, int K,
+                                 const uint8_t* picked, float high, float low, int keep_strong, int update_gate,
+                                 const float* d_logits, const uint8_t* d_gates, const int64_t* d_a,
+                                 const int64_t* d_b, uint8_t* changed, float* m1, float* m2, int32_t* counter,
+                                 cudaStream_t s);
+
 // Error / launch bookkeeping of the C ABI (capi.cu), for entry points defined in other files.
 int set_error(int code, const char* msg);
 void count_launches(int n);

@@ -342,6 +342,23 @@ int clb_entropy_monitor(const float* logits, int64_t rows, int64_t K, float ema_
                         int first, float* ema, int32_t* counter, uint8_t* converged, int32_t* n_converged,
                         clb_stream_t stream);
 
+/* Row resampling of LogicLayer.resample_connections (compactlogic/compactlogic.py:282-368) for the rows with
+ * picked[r] != 0, in place, from caller-drawn random tensors of full size (so the row counts never reach the
+ * host): draw_logits fp32 (N(0,1)), draw_gates uint8 (gate ids in [0, 16)), draw_a / draw_b int64 (inputs in
+ * [0, in_dim)), all [rows, K].  Weak rows (max prob < threshold_low) take new logits, gates and inputs in
+ * every slot; strong rows (max prob > threshold_high) keep their first argmax slot with logit
+ * log(p (K-1) / (1-p)) (p clamped to [1e-6, 1-1e-6]; log(9 (K-1)) without keep_strong_weights), zero the
+ * other logits and give those slots new gates and inputs.  Gates change only with update_gate.  changed[r]
+ * (uint8) marks weak or strong rows; exp_avg / exp_avg_sq (optional, fp32 [rows, K], the optimizer's Adam
+ * moments) are zeroed on changed rows (compactlogic.py:1152-1180); counter (optional, int32 [rows]) is reset
+ * on every picked row (compactlogic.py:1146).  logits fp32 [rows, K], gates uint8 [rows, K], idx_a / idx_b
+ * the two int64 [rows, K] halves of `indices`; K <= 32. */
+int clb_resample_rows(float* logits, uint8_t* gates, int64_t* idx_a, int64_t* idx_b, int64_t rows, int64_t K,
+                      const uint8_t* picked, float threshold_high, float threshold_low, int keep_strong_weights,
+                      int update_gate, const float* draw_logits, const uint8_t* draw_gates, const int64_t* draw_a,
+                      const int64_t* draw_b, uint8_t* changed, float* exp_avg, float* exp_avg_sq, int32_t* counter,
+                      clb_stream_t stream);
+
 /* ---- bit-packed discrete inference (uint64 words, bit i of word w = sample 64 w + i) ---- */
 
 /* x [batch, features] sample-major with values in {0,1} (bit = x > 0.5) -> out [features, ldw]. */

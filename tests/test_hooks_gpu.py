@@ -15,6 +15,7 @@ def _run(model, use_device, steps=40):
     opt = torch.optim.Adam(model.parameters(), lr=0.05)
     rs = cl.EntropyRowResampler(model, ema_decay=0.8, eps=2e-3, patience=3, threshold_low=0.3, threshold_high=0.6)
     rs.use_device_monitor = use_device
+    rs.use_device_resample = False  # same RNG consumption on both sides: only the monitor differs
     torch.cuda.manual_seed(123)
     gen = torch.Generator(device="cuda").manual_seed(5)
     for it in range(steps):
