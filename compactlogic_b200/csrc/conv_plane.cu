@@ -253,8 +253,21 @@ __global__ void __launch_bounds__(kThreads) conv_plane_forward_kernel(const Plan
             const int2* of = off + t * K;
             const float4* cc = cf + t * K;
             const int n = ns[t];
-#pragma unroll 4
-            for (int s = 0; s < n; ++s) {
+            int s = 0;
+            for (; s + 2 <= n; s += 2) {  // the shared loads of two slots issued before their arithmetic
+                const int2 o0 = of[s], o1 = of[s + 1];
+                const float4 a0 = xb[o0.x * 32], b0 = xb[o0.y * 32], a1 = xb[o1.x * 32], b1 = xb[o1.y * 32];
+                const float4 c = cc[s], d = cc[s + 1];
+                acc.x = fmaf(fmaf(c.z, a0.x, c.y), b0.x, fmaf(c.x, a0.x, acc.x));
+                acc.y = fmaf(fmaf(c.z, a0.y, c.y), b0.y, fmaf(c.x, a0.y, acc.y));
+                acc.z = fmaf(fmaf(c.z, a0.z, c.y), b0.z, fmaf(c.x, a0.z, acc.z));
+                acc.w = fmaf(fmaf(c.z, a0.w, c.y), b0.w, fmaf(c.x, a0.w, acc.w));
+                acc.x = fmaf(fmaf(d.z, a1.x, d.y), b1.x, fmaf(d.x, a1.x, acc.x));
+                acc.y = fmaf(fmaf(d.z, a1.y, d.y), b1.y, fmaf(d.x, a1.y, acc.y));
+                acc.z = fmaf(fmaf(d.z, a1.z, d.y), b1.z, fmaf(d.x, a1.z, acc.z));
+                acc.w = fmaf(fmaf(d.z, a1.w, d.y), b1.w, fmaf(d.x, a1.w, acc.w));
+            }
+            for (; s < n; ++s) {
                 const int2 o = of[s];
                 const float4 c = cc[s];
                 const float4 va = xb[o.x * 32], vb = xb[o.y * 32];
@@ -334,7 +347,8 @@ __global__ void __launch_bounds__(kThreads) conv_plane_backward_kernel(const Pla
     int2* off = reinterpret_cast<int2*>(cf + a.cg * KT);
     float* pw = reinterpret_cast<float*>(off + a.cg * KT);
     float* spart = pw + a.cg * KT;
-    int* chan = reinterpret_cast<int*>(spart + a.cg * KT);
+    int2* rcs = reinterpret_cast<int2*>(spart + a.cg * KT);  // (dh+pad, dw+pad) of operand a | b, packed 16:16
+    int* chan = reinterpret_cast<int*>(rcs + a.cg * KT);
 
     const int ty = blockIdx.x / a.tiles_x, tx = blockIdx.x - ty * a.tiles_x;
     const int oy0 = ty * a.TH, ox0 = tx * a.TW;
@@ -380,6 +394,7 @@ __global__ void __launch_bounds__(kThreads) conv_plane_backward_kernel(const Pla
             const GatePoly gp = gate_poly(a.gates[ia] & 15);
             const bool ua = gp.c1 != 0.f || gp.c3 != 0.f, ub = gp.c2 != 0.f || gp.c3 != 0.f;
             off[e] = make_int2(ua ? rel_off(a, a.oh[ia], a.ow[ia]) : -1, ub ? rel_off(a, a.oh[ib], a.ow[ib]) : -1);
+            rcs[e] = make_int2(((a.oh[ia] + a.pad) << 16) | (a.ow[ia] + a.pad), ((a.oh[ib] + a.pad) << 16) | (a.ow[ib] + a.pad));
             cf[e] = make_float4(gp.c0, gp.c1, gp.c2, gp.c3);
             pw[e] = p;
             spart[e] = 0.f;
@@ -400,6 +415,7 @@ __global__ void __launch_bounds__(kThreads) conv_plane_backward_kernel(const Pla
             const int oy = oy0 + oyl, ox = ox0 + oxl;
             if (oy >= a.h_out || ox >= a.w_out) continue;
             const int base = oyl * a.stride * a.TWI + oxl * a.stride;
+            const int by = iy0 + oyl * a.stride, bx = ix0 + oxl * a.stride;  // input coordinates of offset (0, 0)
             float4 g = zero4;
             if (active) g = *reinterpret_cast<const float4*>(gy + ((int64_t)chan[t] * hw + (int64_t)oy * a.w_out + ox) * ldgy + col);
             const int2* of = off + t * KT;
@@ -430,15 +446,16 @@ __global__ void __launch_bounds__(kThreads) conv_plane_backward_kernel(const Pla
                 }
                 pk[k] += dot;
                 if (GX && active) {  // activation gradient straight into L2 (fire-and-forget vector reductions)
+                    const int2 rc = rcs[t * KT + k];
                     if (o.x >= 0) {
-                        const int iy = iy0 + (base + o.x) / a.TWI, ix = ix0 + (base + o.x) % a.TWI;
-                        if (iy >= 0 && iy < a.h_in && ix >= 0 && ix < a.w_in)
-                            red_add<4>(gplane + ((int64_t)iy * a.w_in + ix) * ldgx, da);
+                        const int iy = by + (rc.x >> 16), ix = bx + (rc.x & 0xffff);
+                        if ((unsigned)iy < (unsigned)a.h_in && (unsigned)ix < (unsigned)a.w_in)
+                            red_add<4>(gplane + (int64_t)(iy * a.w_in + ix) * ldgx, da);
                     }
                     if (o.y >= 0) {
-                        const int iy = iy0 + (base + o.y) / a.TWI, ix = ix0 + (base + o.y) % a.TWI;
-                        if (iy >= 0 && iy < a.h_in && ix >= 0 && ix < a.w_in)
-                            red_add<4>(gplane + ((int64_t)iy * a.w_in + ix) * ldgx, db);
+                        const int iy = by + (rc.y >> 16), ix = bx + (rc.y & 0xffff);
+                        if ((unsigned)iy < (unsigned)a.h_in && (unsigned)ix < (unsigned)a.w_in)
+                            red_add<4>(gplane + (int64_t)(iy * a.w_in + ix) * ldgx, db);
                     }
                 }
             }
@@ -485,7 +502,7 @@ size_t fwd_smem(const Geometry& g, int cg, int K) {
 size_t bwd_smem(const Geometry& g, int cg, int K, bool gx) {
     (void)gx;
     return (size_t)(g.THI * g.TWI + 1) * kRowBytes + 16 +
-           (size_t)cg * K * (16 + 8 + 4 + 4) + (size_t)cg * 4;
+           (size_t)cg * K * (16 + 8 + 4 + 4 + 8) + (size_t)cg * 4;
 }
 
 constexpr size_t kMaxSmem = 200 * 1024;
