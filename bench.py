@@ -166,11 +166,11 @@ _L2 = {}
 
 def l2_peaks(dev):
     """GB/s of 512-byte row gathers (mode 0) and gathers + vector reductions (mode 1) at hashed rows of
-    two 32.8 MB slabs (64000 rows = one 128-column chunk of a c2 layer's x and grad_x), best of 5."""
+    two 33.5 MB slabs (65536 rows, about one 128-column chunk of a c2 layer's x and grad_x), best of 5."""
     if _L2:
         return _L2
     from compactlogic_b200 import _lib as L
-    rows, ctas, iters = 64000, 148 * 8, 2000
+    rows, ctas, iters = 65536, 148 * 8, 2000
     src = torch.rand(rows, 128, device=dev)
     dst = torch.zeros(rows, 128, device=dev)
     sink = torch.zeros(1, device=dev)

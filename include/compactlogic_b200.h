@@ -254,7 +254,7 @@ int clb_conv_plane_backward(int dtype, const void* x, int64_t ldx, int64_t ncols
 
 /* Measurement helper, no reference counterpart: throughput probe of the soft kernels' access pattern
  * (512-byte row gathers at hashed rows, mode 0; plus as many 512-byte red.global.add.v4.f32 row
- * reductions, mode 1) over src / dst slabs of `rows` rows; `ctas` CTAs of 256 threads, `iters` steps
+ * reductions, mode 1) over src / dst slabs of `rows` rows (a power of two); `ctas` CTAs of 256 threads, `iters` steps
  * per warp; sink is a device float the loads are kept live through.  The benchmark sizes the slabs
  * like one column chunk of a layer and reports the kernels' L2 traffic against it. */
 int clb_l2_probe(int mode, const float* src, float* dst, int64_t rows, int iters, int ctas, float* sink,
