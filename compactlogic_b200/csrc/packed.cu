@@ -12,6 +12,7 @@
 // carry-save adder tree over 16 words at a time (about 4 logic ops per word instead of 64 bit
 // tests), and the final layer can be fused with it so its outputs are never stored.
 #include <cuda_runtime.h>
+#include <utility>
 
 #include <stdlib.h>
 
@@ -192,6 +193,13 @@ __device__ __forceinline__ uint64_t word_or_zero(const uint64_t* __restrict__ x,
     return idx >= 0 ? __ldg(x + (int64_t)idx * ldx + w) : 0ull;
 }
 
+// Programmatic dependent launch: a kernel of the packed chain lets the next one be scheduled as soon as
+// all its CTAs have started (launch_dependents), and waits for its predecessor's completion and memory
+// (wait) only after the prologue that reads nothing the predecessor writes.  Both are no-ops when the
+// kernel was not launched with the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // One packed layer.  Each lane owns V consecutive word columns (V = 2: one 16-byte load per operand),
 // TW lanes span TW*V columns, 32/TW neurons share a warp row, and each thread handles R neurons
 // spaced 32/TW apart so that 2R independent loads are in flight per thread.
@@ -253,6 +261,7 @@ packed_layer_pipe_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nw
     const int64_t npw = 32 >> tw_log2;
     const int64_t warp_global = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) >> 5;
     const int64_t stride = (((int64_t)gridDim.y * blockDim.x) >> 5) * npw * R;
+    pdl_trigger();
     if (w >= nwords) return;
     const int64_t sub = lane >> tw_log2;
     int64_t base = warp_global * npw * R;
@@ -264,6 +273,7 @@ packed_layer_pipe_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nw
         ab[q] = j < n_out ? sel_ab[j] : make_int2(-1, -1);
         g[q] = j < n_out ? sel_gate[j] : 0;
     }
+    pdl_wait();  // the operand rows are the previous layer's output
     for (; base < n_out; base += stride) {
         Vw va[R], vb[R];
 #pragma unroll
@@ -372,6 +382,8 @@ count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int6
     const int64_t c = blockIdx.y / plan.groups;
     const int64_t seg = (blockIdx.y - c * plan.groups) * S + sl;
     const int64_t w = (int64_t)blockIdx.x * TW + wl;
+    pdl_trigger();
+    pdl_wait();
     VCounter vc;
     if (w < nwords && seg < plan.nseg) {
         const int64_t r0 = c * class_size + seg * plan.seg_len;
@@ -422,12 +434,39 @@ count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int6
 // counts[(sample0 + n) * k + c] += sum_g partial[c * groups + g][n]   (one writer per element)
 __global__ void sum_partials_kernel(const int32_t* __restrict__ partial, int64_t row, int64_t groups, int64_t k,
                                     int32_t* __restrict__ counts, int64_t sample0, int64_t samples) {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < samples * k; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t c = e / samples, n = e - c * samples;
         int32_t v = 0;
         for (int64_t g = 0; g < groups; ++g) v += partial[(c * groups + g) * row + n];
         counts[(sample0 + n) * k + c] += v;
     }
+}
+
+// Launch with the programmatic-serialization attribute when CLB_PACKED_PDL is on (default) so consecutive
+// kernels of a packed pass overlap launch latency and ramp-up with their predecessor's tail.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("CLB_PACKED_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... Exp, typename... Act>
+void launch_chain(void (*kern)(Exp...), dim3 grid, dim3 block, cudaStream_t s, Act&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kern, std::forward<Act>(args)...);
 }
 
 unsigned grid_for(int64_t threads) {
@@ -472,9 +511,11 @@ cudaError_t launch_count(const Src& src, int64_t rows, int64_t nwords, int64_t k
     }
     if (k * p.groups > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)tiles, (unsigned)(k * p.groups));
-    count_kernel<Src><<<grid, 256, 0, s>>>(src, rows, nwords, k, class_size, p, counts, sample0, samples, partial);
+    launch_chain(count_kernel<Src>, grid, dim3(256), s, src, rows, nwords, k, class_size, p, counts, sample0, samples,
+                 partial);
     if (partial != nullptr) {
-        sum_partials_kernel<<<grid_for(samples * k), 256, 0, s>>>(partial, row, p.groups, k, counts, sample0, samples);
+        launch_chain(sum_partials_kernel, dim3(grid_for(samples * k)), dim3(256), s, (const int32_t*)partial, row,
+                     p.groups, k, counts, sample0, samples);
     }
     return cudaGetLastError();
 }
@@ -556,9 +597,11 @@ void packed_layer_go(dim3 grid, cudaStream_t s, int minb, const uint64_t* x, int
         const int64_t cap = std::max<int64_t>(1, (int64_t)sm_count() * (minb == 4 ? 4 : 2) * pipe / grid.x);
         grid.y = (unsigned)std::min<int64_t>(grid.y, cap);
         if (minb == 4)
-            packed_layer_pipe_kernel<R, V, 4><<<grid, 256, 0, s>>>(x, ldx, nwords, ab, g, n_out, y, ldy, tw_log2);
+            launch_chain(packed_layer_pipe_kernel<R, V, 4>, grid, dim3(256), s, x, ldx, nwords, ab, g, n_out, y, ldy,
+                         tw_log2);
         else
-            packed_layer_pipe_kernel<R, V, 1><<<grid, 256, 0, s>>>(x, ldx, nwords, ab, g, n_out, y, ldy, tw_log2);
+            launch_chain(packed_layer_pipe_kernel<R, V, 1>, grid, dim3(256), s, x, ldx, nwords, ab, g, n_out, y, ldy,
+                         tw_log2);
         return;
     }
     if (minb == 4)
