@@ -350,8 +350,32 @@ class LogicLayer(torch.nn.Module):
         self.gate_sequence.add_(0)
         if "max_exp_avg_sq" in st:
             st["max_exp_avg_sq"].masked_fill_(changed.bool()[:, None], 0.0)
-        self.refresh_backward_index_device(changed)
+        # the native kernels never read the inverse index: rebuild it when something does (the reference-API
+        # backward, a checkpoint, a device move), applying the pending refreshes in order
+        self.__dict__.setdefault("_csr_pending", []).append(changed)
         return changed
+
+    _CSR_BUFFERS = ("given_x_indices_of_y_start", "given_x_indices_of_y", "given_x_indices_of_gate")
+
+    def _materialize_csr(self) -> None:
+        pending = self.__dict__.get("_csr_pending")
+        if pending:
+            self.__dict__["_csr_pending"] = []
+            for changed in pending:
+                self.refresh_backward_index_device(changed)
+
+    def __getattr__(self, name):
+        if name in LogicLayer._CSR_BUFFERS and self.__dict__.get("_csr_pending"):
+            self._materialize_csr()
+        return super().__getattr__(name)
+
+    def state_dict(self, *args, **kwargs):
+        self._materialize_csr()
+        return super().state_dict(*args, **kwargs)
+
+    def _apply(self, fn, *args, **kwargs):
+        self._materialize_csr()
+        return super()._apply(fn, *args, **kwargs)
 
     @torch.no_grad()
     def refresh_backward_index_device(self, changed: torch.Tensor = None) -> None:

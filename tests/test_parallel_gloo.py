@@ -19,6 +19,30 @@ def _port():
         return s.getsockname()[1]
 
 
+def _spawn(target, world, *args, attempts=2):
+    """Run `target(rank, world, port, *args, q)` on `world` spawned ranks; returns {rank: payload}.  A fresh
+    rendezvous port per attempt: the port is picked free, then released before the ranks bind it, so another
+    process can take it in between; one retry covers that race."""
+    ctx = mp.get_context("spawn")
+    for attempt in range(attempts):
+        port = _port()
+        q = ctx.Queue()
+        procs = [ctx.Process(target=target, args=(r, world, port, *args, q)) for r in range(world)]
+        for p in procs:
+            p.start()
+        try:
+            res = dict(q.get(timeout=120) for _ in range(world))
+        except Exception:
+            res = None
+        for p in procs:
+            p.join(60)
+            if p.is_alive():
+                p.kill()
+        if res is not None and all(p.exitcode == 0 for p in procs):
+            return res
+    raise AssertionError(f"{target.__name__}: ranks failed on {attempts} attempts")
+
+
 def _init(rank, world, port, timeout_s=30):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -35,21 +59,13 @@ def _grad_worker(rank, world, port, q):
     loss = sum(((p @ x) ** 2).sum() * (i + 1) for i, p in enumerate(params))
     loss.backward()
     sync.finish()
-    q.put((rank, [p.grad.clone() for p in params], x))
+    q.put((rank, ([p.grad.clone() for p in params], x)))
     dist.destroy_process_group()
 
 
 def test_grad_allreduce_averages_per_layer():
-    world, port = 2, _port()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = [ctx.Process(target=_grad_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict((r, (g, x)) for r, g, x in (q.get(timeout=120) for _ in range(world)))
-    for p in procs:
-        p.join(60)
-        assert p.exitcode == 0
+    world = 2
+    res = _spawn(_grad_worker, world)
     torch.manual_seed(0)
     params = [torch.randn(5, 4) for _ in range(3)]
     for i, w in enumerate(params):
@@ -69,16 +85,7 @@ def _bcast_worker(rank, world, port, q):
 
 
 def test_broadcast_makes_replicas_identical():
-    world, port = 2, _port()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = [ctx.Process(target=_bcast_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict(q.get(timeout=120) for _ in range(world))
-    for p in procs:
-        p.join(60)
-        assert p.exitcode == 0
+    res = _spawn(_bcast_worker, 2)
     for k in res[0]:
         assert torch.equal(res[0][k], res[1][k]), k
 
@@ -94,16 +101,8 @@ def _gather_worker(rank, world, port, n, q):
 
 @pytest.mark.parametrize("n", [1, 64, 130, 1000])
 def test_shard_and_gather_counts(n):
-    world, port = 2, _port()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, n, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict(q.get(timeout=120) for _ in range(world))
-    for p in procs:
-        p.join(60)
-        assert p.exitcode == 0
+    world = 2
+    res = _spawn(_gather_worker, world, n)
     expect = torch.arange(n, dtype=torch.int32).unsqueeze(1).repeat(1, 3) * (torch.arange(3, dtype=torch.int32) + 1)
     for r in range(world):
         assert torch.equal(res[r], expect)

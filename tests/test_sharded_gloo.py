@@ -58,13 +58,5 @@ def _worker(rank, world, port, q):
 
 
 def test_shard_and_unshard_two_ranks():
-    world, port = 2, _port()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict(q.get(timeout=120) for _ in range(world))
-    for p in procs:
-        p.join(timeout=60)
-    assert res == {0: True, 1: True}
+    from test_parallel_gloo import _spawn
+    assert _spawn(_worker, 2) == {0: True, 1: True}
