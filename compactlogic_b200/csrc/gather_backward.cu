@@ -20,10 +20,14 @@
 // grad_x.
 //
 // Index layout (bytes, each part 256-aligned): starts int32 [in + 1], tmp int2 [2 * n_out * K] (the
-// unsorted fill), recs int2 [2 * n_out * K], cursor int32 [in].
+// unsorted fill), recs int2 [2 * n_out * K], cursor int32 [in], baked 2 x int4 [2 * n_out * K] (rewritten every
+// step by the fp32 path: see bake_kernel).
 #include <cuda_runtime.h>
 #include <float.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "gates.cuh"
@@ -44,6 +48,7 @@ struct IndexParts {
     int2* tmp;
     int2* recs;
     int32_t* cursor;
+    int4* baked;  // per-step records of the fast fp32 path (see bake_kernel)
     size_t bytes;
 };
 
@@ -57,7 +62,8 @@ IndexParts index_parts(void* base, int64_t n_out, int64_t K, int64_t in_features
     p.tmp = reinterpret_cast<int2*>(b + s_starts);
     p.recs = reinterpret_cast<int2*>(b + s_starts + s_recs);
     p.cursor = reinterpret_cast<int32_t*>(b + s_starts + 2 * s_recs);
-    p.bytes = s_starts + 2 * s_recs + s_cursor;
+    p.baked = reinterpret_cast<int4*>(b + s_starts + 2 * s_recs + s_cursor);
+    p.bytes = s_starts + 2 * s_recs + s_cursor + round256(2 * sizeof(int4) * (size_t)(2 * n_out * K));
     return p;
 }
 
@@ -213,6 +219,8 @@ struct GatherArgs {
     const void* probs;
     const int32_t* starts;
     const int2* recs;
+    int4* baked;
+    int2* tmp;  // the build's scratch: owner slot ids of the fast path
     int64_t in_features;
     int64_t n_out;
     int K;
@@ -336,6 +344,125 @@ __global__ void __launch_bounds__(kThreads, U == 4 ? 3 : 1) logic_backward_gathe
     if (active) store_from_acc<Ac, VEC>(reinterpret_cast<Ac*>(a.gx) + (int64_t)row * a.ldgx + col, acc);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Fast fp32 path.  Once per step (after the softmax) every occurrence is baked into a 32-byte record
+//   { element offset of the other operand's row (-1: not read), element offset of its grad_y row,
+//     p * c_self * s, p * c3 * s,                                   (s: the fused GroupSum's grad scale)
+//     and, for the slot's owner occurrence only, the gate seen from the own operand (c0, cs, co, c3) * s,
+//     zero otherwise }
+// and its slot id (-1 when not the owner), so the walk does no decoding, no division, no table lookup and
+// no branch per occurrence: a warp stages 32 records in shared memory (padded with zero records) and reads
+// each as a broadcast, issues the two row gathers of 4 occurrences, then
+//   grad_x[i] += (p c_self + p c3 x_other) * grad_y,   d loss / d p partial += grad_y * f(x_i, x_other)
+// with the 4 partials reduced by a butterfly and stored by the owner's lanes.
+// ---------------------------------------------------------------------------------------------
+__global__ void bake_kernel(const int2* __restrict__ recs, const int32_t* __restrict__ n_valid, int64_t total,
+                            const float* __restrict__ probs, int K, int64_t group, int64_t ldx, int use_gs,
+                            int64_t gs_size, int64_t ldg, float scale, int4* __restrict__ baked,
+                            int* __restrict__ owner_slot) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    // the record array has room for 2 n_out K occurrences; only the first starts[in_features] are filled
+    if (e >= total || e >= (int64_t)*n_valid) return;
+    const int2 rec = recs[e];
+    const int meta = rec.y;
+    const int64_t slot = (uint32_t)meta >> 7;
+    const int64_t j = slot / K, k = slot - j * K;
+    const float p = probs[(group == 1 ? j : j / group) * K + k];
+    const GatePoly gp = gate_poly(meta & 15);
+    const bool side_b = (meta >> 4) & 1, owner = (meta >> 5) & 1, zero = (meta >> 6) & 1, absent = rec.x < 0;
+    const float cs = zero ? 0.f : (side_b ? gp.c2 : gp.c1);
+    const float co = absent ? 0.f : (side_b ? gp.c1 : gp.c2);
+    const float c3 = (zero || absent) ? 0.f : gp.c3;
+    baked[2 * e] = make_int4(absent ? -1 : (int)((int64_t)rec.x * ldx), (int)((use_gs ? j / gs_size : j) * ldg),
+                             __float_as_int(p * cs * scale), __float_as_int(p * c3 * scale));
+    const float d = owner ? scale : 0.f;
+    baked[2 * e + 1] = make_int4(__float_as_int(gp.c0 * d), __float_as_int(cs * d), __float_as_int(co * d),
+                                 __float_as_int(c3 * d));
+    owner_slot[e] = owner ? (int)slot : -1;
+}
+
+template <int kU2>  // occurrences in flight per warp step
+__global__ void __launch_bounds__(kThreads, kU2 == 8 ? 2 : 3) logic_backward_gather2_kernel(
+    const GatherArgs a, const int4* __restrict__ baked, const int* __restrict__ owner_slot) {
+    __shared__ int4 srec[kWarps][2 * 32];
+    __shared__ int sslot[kWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = blockIdx.x * kWarps + warp;
+    if (row >= (int)a.in_features) return;
+    const int chunk = blockIdx.y;
+    const int col = chunk * 128 + lane * 4;
+    const bool active = col < (int)a.ncols;
+    const int lcol = active ? col : 0;  // inactive lanes read column 0; their results are dropped
+    const float* __restrict__ x = reinterpret_cast<const float*>(a.x);
+    const float* __restrict__ gsrc = reinterpret_cast<const float*>(a.gs_grad != nullptr ? a.gs_grad : a.gy);
+    const int rowoff = row * (int)a.ldx;
+    float* part = reinterpret_cast<float*>(a.part);
+    const int64_t pbase = (int64_t)chunk * a.n_out * a.K;
+    const float4 xi = *reinterpret_cast<const float4*>(x + rowoff + lcol);
+    const float xs[4] = {active ? xi.x : 0.f, active ? xi.y : 0.f, active ? xi.z : 0.f, active ? xi.w : 0.f};
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int beg = a.starts[row], end = a.starts[row + 1];
+    for (int base = beg; base < end; base += 32) {
+        const int n = min(32, end - base);
+        __syncwarp();
+        if (lane < n) {
+            srec[warp][2 * lane] = baked[2 * (base + lane)];
+            srec[warp][2 * lane + 1] = baked[2 * (base + lane) + 1];
+            sslot[warp][lane] = owner_slot[base + lane];
+        } else {  // zero records: own row, coefficient 0, no owner
+            srec[warp][2 * lane] = make_int4(-1, 0, 0, 0);
+            srec[warp][2 * lane + 1] = make_int4(0, 0, 0, 0);
+            sslot[warp][lane] = -1;
+        }
+        __syncwarp();
+        for (int e = 0; e < n; e += kU2) {
+            float4 xo[kU2], g[kU2];
+            int4 r[kU2];
+#pragma unroll
+            for (int u = 0; u < kU2; ++u) {
+                r[u] = srec[warp][2 * ((e + u) & 31)];
+                xo[u] = *reinterpret_cast<const float4*>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol);
+                g[u] = *reinterpret_cast<const float4*>(gsrc + r[u].y + lcol);
+            }
+            float dot[kU2];
+#pragma unroll
+            for (int u = 0; u < kU2; ++u) {
+                const int4 cd = srec[warp][2 * ((e + u) & 31) + 1];
+                const float pcs = __int_as_float(r[u].z), pc3 = __int_as_float(r[u].w);
+                const float c0 = __int_as_float(cd.x), cs = __int_as_float(cd.y), co = __int_as_float(cd.z),
+                            c3 = __int_as_float(cd.w);
+                const float o[4] = {xo[u].x, xo[u].y, xo[u].z, xo[u].w}, gg[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
+                float d = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[i] = fmaf(fmaf(pc3, o[i], pcs), gg[i], acc[i]);
+                    d = fmaf(gg[i], fmaf(fmaf(c3, xs[i], co), o[i], fmaf(cs, xs[i], c0)), d);
+                }
+                dot[u] = active ? d : 0.f;
+            }
+            if (part != nullptr) {
+                RS<float, kU2, 16>::run(dot, lane);
+                constexpr int SH = kU2 == 8 ? 2 : 3;  // lanes per reduced value: 32 / kU2
+                const int slot = sslot[warp][(e + ((lane >> SH) & (kU2 - 1))) & 31];
+                if ((lane & ((1 << SH) - 1)) == 0 && slot >= 0) part[pbase + slot] = dot[0];
+            }
+        }
+    }
+    if (active) *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.gx) + (int64_t)row * a.ldgx + col) =
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// The fast path applies to fp32 with 16-byte rows and every element offset below 2^31.
+bool fast_ok(const GatherArgs& a) {
+    static const bool enabled = [] {
+        const char* e = getenv("CLB_GATHER_FAST");
+        return !(e && e[0] == '0');
+    }();
+    const int64_t lim = int64_t(1) << 31;
+    const int64_t gext = a.gs_grad ? (a.n_out / a.gs_size + 1) * a.ld_gs : a.n_out * a.ldgy;
+    return enabled && a.in_features * a.ldx < lim && gext < lim && a.ncols < lim && a.ldgx * a.in_features < lim;
+}
+
 template <typename T> constexpr int gvec() { return 16 / (int)sizeof(T) > 4 ? 4 : 16 / (int)sizeof(T); }
 
 inline bool al(const void* p, int bytes) { return p == nullptr || ((uintptr_t)p % bytes) == 0; }
@@ -403,6 +530,28 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
+    if (std::is_same<T, float>::value && gather_vec<T>(a) == 4 && fast_ok(a)) {
+        const int64_t total = a.starts == nullptr ? 0 : 2 * a.n_out * a.K;
+        if (total > 0) {
+            bake_kernel<<<(unsigned)ceil_div64(total, 256), 256, 0, s>>>(
+                a.recs, a.starts + a.in_features, total, reinterpret_cast<const float*>(a.probs), a.K, a.group, a.ldx, a.gs_grad != nullptr,
+                a.gs_size, a.gs_grad ? a.ld_gs : a.ldgy, (float)(a.gs_grad ? a.gs_scale : 1.0), a.baked,
+                reinterpret_cast<int*>(a.tmp));
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        }
+        dim3 grid((unsigned)ceil_div64(a.in_features, kWarps), (unsigned)ceil_div64(a.ncols, 128));
+        if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+        static const int u2 = [] {
+            const char* e = getenv("CLB_GATHER2_U");
+            return e && atoi(e) == 8 ? 8 : 4;
+        }();
+        if (u2 == 8)
+            logic_backward_gather2_kernel<8><<<grid, kThreads, 0, s>>>(a, a.baked, reinterpret_cast<int*>(a.tmp));
+        else
+            logic_backward_gather2_kernel<4><<<grid, kThreads, 0, s>>>(a, a.baked, reinterpret_cast<int*>(a.tmp));
+        return cudaGetLastError();
+    }
     if (gather_vec<T>(a) == gvec<T>()) return gather_launch_v<T, gvec<T>()>(a, s);
     return gather_launch_v<T, 1>(a, s);
 }
@@ -427,6 +576,8 @@ GatherArgs make_args(const void* x, int64_t ldx, int64_t ncols, const void* gy, 
     a.probs = probs;
     a.starts = ip.starts;
     a.recs = ip.recs;
+    a.baked = ip.baked;
+    a.tmp = ip.tmp;
     a.in_features = in_features;
     a.n_out = n_out;
     a.K = K;
