@@ -56,7 +56,11 @@ C5 = dict(in_dim=3072, width=1_000_000, layers=4, K=4, k=100, tau=30.0, batch=51
 # Checksum of the gathered c4 class counts (sum over samples i and classes of count * (i % 1009 + 1)) for the
 # fixed seeds of build_c4 / c4_words, measured on one B200: every N must reproduce it.
 C4_COUNTS_CHECKSUM = 270315957402565
+#  - logic_backward_gather2_kernel (the default fp32 backward of the 64000->64000 layers): 1.078 GB per launch
+#    (0.797 GB read + 0.281 GB write, profiles/logic_backward_gather_c2.md); the first layer keeps the
+#    scatter kernel without grad_x (0.317 GB);
 NCU_TRAFFIC = {"logic_backward_kernel": (5 * 2.160e9 + 0.317e9) / 6,
+               "logic_backward_gather2_kernel": 1.078e9,
                "packed_pass": 512 * (0.263e9 + 6 * 0.583e9 + 0.343e9)}
 
 
@@ -196,9 +200,12 @@ def roofline(kern, hbm, src, traffic=None, dev=None, extra=None):
         return None
     dom = max(kern, key=lambda k: kern[k][1])
     n, tot_ms, tot_b, tot_l2 = kern[dom]
+    if isinstance(traffic, dict):
+        traffic = traffic.get(dom)
     achieved = tot_b / (tot_ms / 1e3) / 1e9
     total = sum(w[1] for w in kern.values())
     r = {"kernel": {"backward": "logic_backward_kernel", "forward": "logic_forward_kernel",
+                    "backward_gather": "logic_backward_gather2_kernel (+ bake_kernel)",
                     "conv_backward": "conv_plane_backward_kernel", "conv_forward": "conv_plane_forward_kernel"
                     }.get(dom, dom),
          "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "peak_source": src, "unit": "GB/s",
@@ -207,13 +214,15 @@ def roofline(kern, hbm, src, traffic=None, dev=None, extra=None):
          "shares": {k: round(v[1] / total, 3) for k, v in kern.items()}}
     if tot_l2 and dev is not None:
         pk = l2_peaks(dev)
-        key = "gather_reduce" if "backward" in dom else "gather"
+        key = "gather_reduce" if dom in ("backward", "conv_backward") else "gather"
         l2 = tot_l2 / (tot_ms / 1e3) / 1e9
         r["l2"] = {"achieved": round(l2, 1), "peak": pk[key], "unit": "GB/s", "frac": round(l2 / pk[key], 4),
                    "bytes_per_launch": round(tot_l2 / n),
                    "peak_source": f"clb_l2_probe mode {'1 (row gathers + row reductions)' if key == 'gather_reduce' else '0 (row gathers)'}, this run",
-                   "note": "one read per used operand and column (+ one reduction with grad_x); slabs of one "
-                           "128-column chunk stay in L2"}
+                   "note": ("one read of the other operand's row and one of grad_y's per occurrence (used operand) "
+                            "and column; no reductions" if dom == "backward_gather" else
+                            "one read per used operand and column (+ one reduction with grad_x)") +
+                           "; slabs of one 128-column chunk stay in L2"}
     if extra:
         r.update(extra)
     return r
@@ -395,7 +404,9 @@ def bench_c2(args, dev, rank, world, strong=False):
     ms_e2e, e2e = e2e_of(step, x_host, y_host, dev, args.steps, B if width else B * world)
     hbm, src = peaks()
     full = C2["layers"] == 6 and B == 1024 and not width
-    roof = roofline(kern, hbm, src, NCU_TRAFFIC["logic_backward_kernel"] if full else None, dev,
+    roof = roofline(kern, hbm, src, {"backward": NCU_TRAFFIC["logic_backward_kernel"],
+                                     "backward_gather": NCU_TRAFFIC["logic_backward_gather2_kernel"]} if full else None,
+                    dev,
                     {"traffic_note": "ncu dram__bytes_read+write per launch at the c2 shapes, cold cache (profiles/)"})
     step_bytes = c2_bytes_per_step(B)
     gb = B if width else B * world  # strong DP: B = 1024 / world, so gb = 1024

@@ -381,8 +381,8 @@ __global__ void bake_kernel(const int2* __restrict__ recs, const int32_t* __rest
     owner_slot[e] = owner ? (int)slot : -1;
 }
 
-template <int kU2>  // occurrences in flight per warp step
-__global__ void __launch_bounds__(kThreads, kU2 == 8 ? 2 : 3) logic_backward_gather2_kernel(
+template <int kU2, int MINB>  // occurrences in flight per warp step, resident CTAs per SM
+__global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
     const GatherArgs a, const int4* __restrict__ baked, const int* __restrict__ owner_slot) {
     __shared__ int4 srec[kWarps][2 * 32];
     __shared__ int sslot[kWarps][32];
@@ -442,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, kU2 == 8 ? 2 : 3) logic_backward_gat
             }
             if (part != nullptr) {
                 RS<float, kU2, 16>::run(dot, lane);
-                constexpr int SH = kU2 == 8 ? 2 : 3;  // lanes per reduced value: 32 / kU2
+                constexpr int SH = kU2 == 8 ? 2 : kU2 == 4 ? 3 : 4;  // log2(lanes per reduced value) = 5 - log2(kU2)
                 const int slot = sslot[warp][(e + ((lane >> SH) & (kU2 - 1))) & 31];
                 if ((lane & ((1 << SH) - 1)) == 0 && slot >= 0) part[pbase + slot] = dot[0];
             }
@@ -542,14 +542,19 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
         }
         dim3 grid((unsigned)ceil_div64(a.in_features, kWarps), (unsigned)ceil_div64(a.ncols, 128));
         if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-        static const int u2 = [] {
-            const char* e = getenv("CLB_GATHER2_U");
-            return e && atoi(e) == 8 ? 8 : 4;
+        // CLB_GATHER2: occurrences in flight x resident CTAs per SM (tuning; 44 = 4 x 4, the default)
+        static const int cfg = [] {
+            const char* e = getenv("CLB_GATHER2");
+            const int v = e ? atoi(e) : 44;
+            return (v == 43 || v == 25 || v == 26) ? v : 44;
         }();
-        if (u2 == 8)
-            logic_backward_gather2_kernel<8><<<grid, kThreads, 0, s>>>(a, a.baked, reinterpret_cast<int*>(a.tmp));
-        else
-            logic_backward_gather2_kernel<4><<<grid, kThreads, 0, s>>>(a, a.baked, reinterpret_cast<int*>(a.tmp));
+        int* owner = reinterpret_cast<int*>(a.tmp);
+        switch (cfg) {
+            case 43: logic_backward_gather2_kernel<4, 3><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            case 25: logic_backward_gather2_kernel<2, 5><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            case 26: logic_backward_gather2_kernel<2, 6><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            default: logic_backward_gather2_kernel<4, 4><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+        }
         return cudaGetLastError();
     }
     if (gather_vec<T>(a) == gvec<T>()) return gather_launch_v<T, gvec<T>()>(a, s);

@@ -65,14 +65,22 @@ def _plane_ok(spec: "LayerSpec", xt: torch.Tensor, *others) -> bool:
     return B % 4 == 0 and spec.K in (4, 8, 16)
 
 
-def _gather_backward_enabled(spec: "LayerSpec") -> bool:
-    """Whether a layer that needs grad_x uses the gather-form backward (clb_logic_backward_gather:
-    grad_x summed in a fixed order, so bitwise reproducible run to run) instead of the scatter form
-    (clb_logic_backward, whose grad_x reductions land in a hardware-dependent order).  Opt-in with
-    CLB_BWD_GATHER=1: measured on a B200, the gather form is 7 % slower on a 64000-wide fp32 step and
-    level with the scatter form on 1M-wide bf16 layers."""
-    del spec
-    return os.environ.get("CLB_BWD_GATHER", "0") == "1"
+def _gather_backward_enabled(spec: "LayerSpec", xt: torch.Tensor) -> bool:
+    """Whether a layer that needs grad_x uses the gather-form backward (clb_logic_backward_gather: walked by
+    destination, grad_x summed in a fixed order, so bitwise reproducible run to run) instead of the scatter
+    form (clb_logic_backward, whose grad_x reductions land in a hardware-dependent order).
+
+    CLB_BWD_GATHER=1 / 0 forces either form.  By default ("auto") the gather form runs for fp32 dense layers
+    with at least 16384 (input row x 128-column chunk) warps of work: measured on a B200 it is faster there
+    (c2 step 9.33 vs 9.82 ms, c3 2.01 vs 2.17 ms) and slower on small layers (c1: 0.143 vs 0.124 ms) and on
+    bf16 / fp64 activations, which use its unbaked kernel."""
+    mode = os.environ.get("CLB_BWD_GATHER", "auto")
+    if mode in ("0", "1"):
+        return mode == "1"
+    if spec.conv is not None or xt.dtype != torch.float32 or spec.group != 1:
+        return False
+    B = xt.shape[1]
+    return B % 4 == 0 and spec.in_features * -(-B // 128) >= 16384 and spec.n_out * spec.K <= (1 << 24)
 
 
 def layer_index(spec: LayerSpec, device) -> Optional[torch.Tensor]:
@@ -194,7 +202,7 @@ def backward_into(xt: torch.Tensor, weights: torch.Tensor, spec: LayerSpec, mode
                   gy: Optional[torch.Tensor], gs_grad: Optional[torch.Tensor], gs_size: int, gs_scale: float,
                   need_gx: bool, need_gw: bool):
     """Returns (grad_x [in, B] or None, grad_weights [rows, K] or None)."""
-    if need_gx and _gather_backward_enabled(spec) and mode in (L.W_LOGITS, L.W_PROBS):
+    if need_gx and mode in (L.W_LOGITS, L.W_PROBS) and _gather_backward_enabled(spec, xt):
         index = layer_index(spec, xt.device)
         if index is not None:
             return _backward_gather(xt, weights, spec, mode, gy, gs_grad, gs_size, gs_scale, need_gw, index)
@@ -270,10 +278,12 @@ def _backward_gather(xt, weights, spec, mode, gy, gs_grad, gs_size, gs_scale, ne
     a = torch.empty((), dtype=acc).element_size()
     nbytes = (xt.element_size() * B * spec.in_features + (a * B * spec.n_out if gy is not None else 0) +
               a * B * spec.in_features + _param_bytes(spec))
-    TIMER.launch("backward", nbytes, lambda: L.call(
+    # L2 bytes: per occurrence (used operand) one read of the other operand's row and one of grad_y's
+    l2 = used_operands(spec) * B * (xt.element_size() + a) if TIMER.enabled else 0
+    TIMER.launch("backward_gather", nbytes, lambda: L.call(
         "clb_logic_backward_gather", L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), B, spec.in_features,
         spec.n_out, spec.K, spec.group, mode, L.ptr(weights), L.ptr(index), gy_ptr, ldgy, gs_ptr, gs_k, gs_size,
-        ld_gs, float(gs_scale), L.ptr(gx), B, L.ptr(probs), L.ptr(part), chunks if need_gw else 0, L.stream(dev)))
+        ld_gs, float(gs_scale), L.ptr(gx), B, L.ptr(probs), L.ptr(part), chunks if need_gw else 0, L.stream(dev)), l2)
     gw = None
     if need_gw:
         gw = torch.empty(spec.n_out // spec.group, spec.K, dtype=acc, device=dev)

@@ -268,7 +268,9 @@ int clb_l2_probe(int mode, const float* src, float* dst, int64_t rows, int iters
  * logic_layer_cuda_backward_w, difflogic_kernel.cu:82-137).  One warp per input row and column chunk
  * gathers, for each occurrence, the other operand and grad_y of the slot's neuron; grad_x is stored once
  * (not accumulated, not atomically), and its summation order is fixed for a given index.
- * Requires n_out * K <= 2^24. */
+ * For fp32 with 16-byte rows and element offsets below 2^31 each call first bakes every occurrence into a
+ * 32-byte record (offsets, p-scaled coefficients, the owner's gate) stored in the index buffer, so the index
+ * must not be shared by calls that overlap on the GPU.  Requires n_out * K <= 2^24. */
 
 /* Bytes of a layer's occurrence index (-1 if the sizes are out of range). */
 int64_t clb_logic_index_bytes(int64_t n_out, int64_t K, int64_t in_features);

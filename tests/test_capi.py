@@ -45,7 +45,8 @@ def test_gather_backward_index_sizes_and_argument_checks():
     L = _lib.lib()
     r256 = lambda v: (v + 255) // 256 * 256
     n_out, K, inf = 64000, 16, 64000
-    assert L.clb_logic_index_bytes(n_out, K, inf) == r256(4 * (inf + 1)) + 2 * r256(8 * 2 * n_out * K) + r256(4 * inf)
+    assert L.clb_logic_index_bytes(n_out, K, inf) == (r256(4 * (inf + 1)) + 2 * r256(8 * 2 * n_out * K) + r256(4 * inf) +
+                                                    r256(32 * 2 * n_out * K))  # + the per-step baked records
     assert L.clb_logic_index_bytes(1 << 20, 16, 10) > 0                  # 2^24 slots: at the limit
     assert L.clb_logic_index_bytes((1 << 20) + 1, 16, 10) == -1          # slot id field overflow
     assert L.clb_logic_index_bytes(10, 0, 10) == -1
