@@ -1043,7 +1043,14 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        # NCCL on a high-priority stream: its kernels get SMs as soon as any frees up, so the per-layer
+        # gradient buckets overlap the backward instead of queueing behind the layer kernels' full grids
+        # (CLB_NCCL_HIPRI=0: default priority)
+        opts = None
+        if os.environ.get("CLB_NCCL_HIPRI", "1") != "0":
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+        dist.init_process_group("nccl", device_id=dev, pg_options=opts)
     cpu = rank == 0 and world == 1 and not args.no_cpu
     cpu_sub = args.cpu_budget / 2
 

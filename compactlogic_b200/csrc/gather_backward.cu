@@ -381,7 +381,7 @@ __global__ void bake_kernel(const int2* __restrict__ recs, const int32_t* __rest
     owner_slot[e] = owner ? (int)slot : -1;
 }
 
-template <int kU2, int MINB>  // occurrences in flight per warp step, resident CTAs per SM
+template <typename T, int kU2, int MINB>  // activation type, occurrences in flight per warp step, CTAs per SM
 __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
     const GatherArgs a, const int4* __restrict__ baked, const int* __restrict__ owner_slot) {
     __shared__ int4 srec[kWarps][2 * 32];
@@ -393,13 +393,15 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
     const int col = chunk * 128 + lane * 4;
     const bool active = col < (int)a.ncols;
     const int lcol = active ? col : 0;  // inactive lanes read column 0; their results are dropped
-    const float* __restrict__ x = reinterpret_cast<const float*>(a.x);
+    const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
     const float* __restrict__ gsrc = reinterpret_cast<const float*>(a.gs_grad != nullptr ? a.gs_grad : a.gy);
     const int rowoff = row * (int)a.ldx;
     float* part = reinterpret_cast<float*>(a.part);
     const int64_t pbase = (int64_t)chunk * a.n_out * a.K;
-    const float4 xi = *reinterpret_cast<const float4*>(x + rowoff + lcol);
-    const float xs[4] = {active ? xi.x : 0.f, active ? xi.y : 0.f, active ? xi.z : 0.f, active ? xi.w : 0.f};
+    float xs[4];
+    load_acc<T, 4>(x + rowoff + lcol, xs);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) xs[i] = active ? xs[i] : 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const int beg = a.starts[row], end = a.starts[row + 1];
     for (int base = beg; base < end; base += 32) {
@@ -416,12 +418,13 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
         }
         __syncwarp();
         for (int e = 0; e < n; e += kU2) {
-            float4 xo[kU2], g[kU2];
+            float xo[kU2][4];
+            float4 g[kU2];
             int4 r[kU2];
 #pragma unroll
             for (int u = 0; u < kU2; ++u) {
                 r[u] = srec[warp][2 * ((e + u) & 31)];
-                xo[u] = *reinterpret_cast<const float4*>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol);
+                load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
                 g[u] = *reinterpret_cast<const float4*>(gsrc + r[u].y + lcol);
             }
             float dot[kU2];
@@ -431,7 +434,8 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
                 const float pcs = __int_as_float(r[u].z), pc3 = __int_as_float(r[u].w);
                 const float c0 = __int_as_float(cd.x), cs = __int_as_float(cd.y), co = __int_as_float(cd.z),
                             c3 = __int_as_float(cd.w);
-                const float o[4] = {xo[u].x, xo[u].y, xo[u].z, xo[u].w}, gg[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
+                const float* o = xo[u];
+                const float gg[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
                 float d = 0.f;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -452,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
         make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
 
-// The fast path applies to fp32 with 16-byte rows and every element offset below 2^31.
+// The fast (baked) path applies to fp32 / bf16 / fp16 activations with whole 4-column vectors and every element offset below 2^31.
 bool fast_ok(const GatherArgs& a) {
     static const bool enabled = [] {
         const char* e = getenv("CLB_GATHER_FAST");
@@ -530,7 +534,7 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    if (std::is_same<T, float>::value && gather_vec<T>(a) == 4 && fast_ok(a)) {
+    if constexpr (!std::is_same<T, double>::value) if (gather_vec<T>(a) == 4 && fast_ok(a)) {
         const int64_t total = a.starts == nullptr ? 0 : 2 * a.n_out * a.K;
         if (total > 0) {
             bake_kernel<<<(unsigned)ceil_div64(total, 256), 256, 0, s>>>(
@@ -550,10 +554,10 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
         }();
         int* owner = reinterpret_cast<int*>(a.tmp);
         switch (cfg) {
-            case 43: logic_backward_gather2_kernel<4, 3><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
-            case 25: logic_backward_gather2_kernel<2, 5><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
-            case 26: logic_backward_gather2_kernel<2, 6><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
-            default: logic_backward_gather2_kernel<4, 4><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            case 43: logic_backward_gather2_kernel<T, 4, 3><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            case 25: logic_backward_gather2_kernel<T, 2, 5><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            case 26: logic_backward_gather2_kernel<T, 2, 6><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            default: logic_backward_gather2_kernel<T, 4, 4><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
         }
         return cudaGetLastError();
     }

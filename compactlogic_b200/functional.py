@@ -70,14 +70,14 @@ def _gather_backward_enabled(spec: "LayerSpec", xt: torch.Tensor) -> bool:
     destination, grad_x summed in a fixed order, so bitwise reproducible run to run) instead of the scatter
     form (clb_logic_backward, whose grad_x reductions land in a hardware-dependent order).
 
-    CLB_BWD_GATHER=1 / 0 forces either form.  By default ("auto") the gather form runs for fp32 dense layers
-    with at least 16384 (input row x 128-column chunk) warps of work: measured on a B200 it is faster there
-    (c2 step 9.33 vs 9.82 ms, c3 2.01 vs 2.17 ms) and slower on small layers (c1: 0.143 vs 0.124 ms) and on
-    bf16 / fp64 activations, which use its unbaked kernel."""
+    CLB_BWD_GATHER=1 / 0 forces either form.  By default ("auto") the gather form runs for fp32 / bf16 / fp16
+    dense layers with at least 16384 (input row x 128-column chunk) warps of work: measured on a B200 it is
+    faster there (c2 step 9.33 vs 9.82 ms, c3 2.01 vs 2.17 ms, c5 bf16 20.4 vs 26.0 ms) and slower on small
+    layers (c1: 0.143 vs 0.124 ms) and on fp64, which uses its unbaked kernel."""
     mode = os.environ.get("CLB_BWD_GATHER", "auto")
     if mode in ("0", "1"):
         return mode == "1"
-    if spec.conv is not None or xt.dtype != torch.float32 or spec.group != 1:
+    if spec.conv is not None or xt.dtype == torch.float64 or spec.group != 1:
         return False
     B = xt.shape[1]
     return B % 4 == 0 and spec.in_features * -(-B // 128) >= 16384 and spec.n_out * spec.K <= (1 << 24)

@@ -131,3 +131,20 @@ def test_conv_both_backward_forms(gather, monkeypatch):
 def test_index_rejects_oversize():
     assert L.lib().clb_logic_index_bytes(1 << 21, 16, 100) == -1
     assert L.lib().clb_logic_index_build(None, 1 << 21, 16, 1, None, 100, None, 0, None) == L.CLB_ERR_INVALID
+
+
+@pytest.mark.parametrize("in_dim,out,K,B", [(784, 512, 16, 256), (300, 1000, 4, 128), (64, 64, 8, 36)])
+def test_gather_bf16_vs_oracle_and_scatter(in_dim, out, K, B, monkeypatch):
+    """bf16 activations (fp32 gradients) on the baked gather path, against the oracle on the bf16-rounded
+    input and against the scatter form."""
+    x, a, b, logits, g, gy = rand_dense(in_dim + 5 * K + B, in_dim, out, K, B)
+    xr = torch.from_numpy(x).to(torch.bfloat16).double().numpy()
+    gy = torch.from_numpy(gy).to(torch.bfloat16).double().numpy()  # autograd hands the bf16 output a bf16 gradient
+    spec = _spec(a, b, g, in_dim)
+    gx, gw = _grads(x, logits, spec, gy, torch.bfloat16, True, monkeypatch)
+    assert spec.index is not None, "gather path not taken"
+    p = O.softmax(logits)
+    assert_close(gx, O.dense_backward_x(xr, a, b, p, g, gy), RTOL[torch.bfloat16], "grad_x")
+    assert_close(gw, O.softmax_backward(p, O.dense_backward_w(xr, a, b, g, gy)), 1e-4, "grad_logits")
+    gx_s, gw_s = _grads(x, logits, spec, gy, torch.bfloat16, False, monkeypatch)
+    assert_close(gw, gw_s.double().cpu().numpy(), 1e-4, "grad_logits vs scatter")
