@@ -370,8 +370,11 @@ def bench_c2(args, dev, rank, world, strong=False):
         model = shard_width(model)
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.Adam(params, lr=0.01, fused=True)
-    sync = None if width else GradAllReduce(params)
     strong = strong and not width
+    # per-layer buckets overlap a long backward (1024 per GPU); one flat bucket after a short one (strong
+    # scaling at 1024/N per GPU, see GradAllReduce)
+    sync = None if width else GradAllReduce(params, bucket=os.environ.get("CLB_DP_BUCKET",
+                                                                          "flat" if strong and world > 2 else "layer"))
     B = C2["batch"] // world if strong else C2["batch"]
     x_host, y_host = c2_inputs(1000 + (0 if width else rank), B)
     x_dev, y_dev = x_host.to(dev), y_host.to(dev)
@@ -438,8 +441,11 @@ def bench_c2(args, dev, rank, world, strong=False):
             torch.cuda.synchronize(dev)
             t = statistics.median(s.elapsed_time(e) for s, e in evs)
             res["limiter"] = {"allreduce_tail_ms": round(t, 4), "share_of_step": round(t / ms, 4),
-                              "what": "wait for the last per-layer gradient bucket after the last backward kernel "
-                                      "(the first layer's bucket has no backward work left to overlap)"}
+                              "bucket": sync.bucket,
+                              "what": ("wait for the last per-layer gradient bucket after the last backward kernel "
+                                       "(the first layer's bucket has no backward work left to overlap)")
+                              if sync.bucket == "layer" else
+                              "one all-reduce of all gate-logit gradients (24.6 MB) after the backward"}
     return res, model
 
 
@@ -1043,14 +1049,7 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
-        # NCCL on a high-priority stream: its kernels get SMs as soon as any frees up, so the per-layer
-        # gradient buckets overlap the backward instead of queueing behind the layer kernels' full grids
-        # (CLB_NCCL_HIPRI=0: default priority)
-        opts = None
-        if os.environ.get("CLB_NCCL_HIPRI", "1") != "0":
-            opts = dist.ProcessGroupNCCL.Options()
-            opts.is_high_priority_stream = True
-        dist.init_process_group("nccl", device_id=dev, pg_options=opts)
+        dist.init_process_group("nccl", device_id=dev)
     cpu = rank == 0 and world == 1 and not args.no_cpu
     cpu_sub = args.cpu_budget / 2
 

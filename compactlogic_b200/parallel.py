@@ -20,19 +20,28 @@ import torch.distributed as dist
 
 
 class GradAllReduce:
-    """Per-layer, overlapped all-reduce of the gradients of ``params``.
+    """All-reduce of the gradients of ``params``.
+
+    ``bucket="layer"`` (default): one all-reduce per parameter, launched from a post-accumulate hook the
+    moment its backward finishes, overlapping the backward of the layers below — the choice when each
+    layer's backward is long (large per-GPU batch).  ``bucket="flat"``: one all-reduce of all gradients,
+    concatenated, after the backward — the choice for small per-GPU batches, where the layer kernels fill
+    every SM and concurrent per-layer collectives only queue behind them (measured on 8 B200s at 128
+    samples per GPU: all-reduce of 4.1 MB 59 us, of the whole 24.6 MB 126 us, but an un-overlapped tail
+    of 0.47-1.29 ms with per-layer buckets).
 
     Usage per step: loss.backward(); sync.finish(); clip; optimizer.step().
     """
 
-    def __init__(self, params, group=None, average: bool = True):
+    def __init__(self, params, group=None, average: bool = True, bucket: str = "layer"):
         self.params: List[torch.nn.Parameter] = [p for p in params if p.requires_grad]
         self.group = group
         self.average = average
+        self.bucket = bucket
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self._works = []
         self._handles = []
-        if self.world > 1:
+        if self.world > 1 and bucket == "layer":
             for p in self.params:
                 self._handles.append(p.register_post_accumulate_grad_hook(self._hook))
 
@@ -43,6 +52,16 @@ class GradAllReduce:
 
     def finish(self):
         """Wait for all buckets of this step and average them."""
+        if self.world > 1 and self.bucket == "flat":
+            grads = [p.grad for p in self.params if p.grad is not None]
+            if grads:
+                flat = torch.cat([g.reshape(-1) for g in grads])
+                dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+                if self.average:
+                    flat.div_(self.world)
+                for g, v in zip(grads, flat.split([g.numel() for g in grads])):
+                    g.copy_(v.view_as(g))
+            return
         works, self._works = self._works, []
         for p, w in works:
             w.wait()

@@ -140,3 +140,31 @@ def test_missing_rank_raises_bounded_error():
     for p in procs:
         p.join(60)
     assert rank == 0 and outcome != "no error"
+
+
+def _flat_worker(rank, world, port, q):
+    _init(rank, world, port)
+    torch.manual_seed(0)
+    params = [torch.nn.Parameter(torch.randn(5, 4)) for _ in range(3)]
+    res = {}
+    for bucket in ("layer", "flat"):
+        for p in params:
+            p.grad = None
+        sync = P.GradAllReduce(params, bucket=bucket)
+        torch.manual_seed(100 + rank)
+        x = torch.randn(4, 7)
+        sum(((p @ x) ** 2).sum() * (i + 1) for i, p in enumerate(params)).backward()
+        sync.finish()
+        sync.remove()
+        res[bucket] = [p.grad.clone() for p in params]
+    q.put((rank, res))
+    dist.destroy_process_group()
+
+
+def test_flat_bucket_equals_per_layer_buckets():
+    res = _spawn(_flat_worker, 2)
+    for r in range(2):
+        for a, b in zip(res[r]["layer"], res[r]["flat"]):
+            torch.testing.assert_close(a, b)
+        for a, b in zip(res[r]["flat"], res[0]["flat"]):
+            assert torch.equal(a, b)
