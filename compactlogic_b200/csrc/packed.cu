@@ -67,6 +67,25 @@ struct VCounter {
             carry = t;
         }
     }
+    // Add 8 words (the carry out of the 8s plane is a half-adder step).
+    __device__ __forceinline__ void add8(const uint64_t (&d)[8]) {
+        uint64_t twosA, twosB, foursA, foursB, eightsA;
+        csa(twosA, ones, ones, d[0], d[1]);
+        csa(twosB, ones, ones, d[2], d[3]);
+        csa(foursA, twos, twos, twosA, twosB);
+        csa(twosA, ones, ones, d[4], d[5]);
+        csa(twosB, ones, ones, d[6], d[7]);
+        csa(foursB, twos, twos, twosA, twosB);
+        csa(eightsA, fours, fours, foursA, foursB);
+        uint64_t carry = eights & eightsA;
+        eights ^= eightsA;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const uint64_t t = hi[p] & carry;
+            hi[p] ^= carry;
+            carry = t;
+        }
+    }
     // 8x8 bit-matrix transpose: in byte r / bit c -> out byte c / bit r.
     static __device__ __forceinline__ uint64_t transpose8x8(uint64_t x) {
         uint64_t t;
@@ -246,10 +265,34 @@ packed_layer_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords,
     }
 }
 
+// Stores of a packed layer's output words.  ST = 0: plain store.  ST = 1: store under an L2 evict-first
+// cache policy, so the 262 MB of freshly written output (read again only by the next launch) displaces
+// less of the operand slab that this launch is still gathering from.
+template <int ST, int V>
+__device__ __forceinline__ void store_words(uint64_t* p, const Vec<uint64_t, V>& o, uint64_t policy) {
+    if constexpr (ST == 1 && V == 2) {
+        asm volatile("st.global.L2::cache_hint.v2.u64 [%0], {%1, %2}, %3;" ::"l"(p), "l"(o.v[0]), "l"(o.v[1]),
+                     "l"(policy)
+                     : "memory");
+    } else if constexpr (ST == 1) {
+#pragma unroll
+        for (int i = 0; i < V; ++i)
+            asm volatile("st.global.L2::cache_hint.u64 [%0], %1, %2;" ::"l"(p + i), "l"(o.v[i]), "l"(policy) : "memory");
+    } else {
+        *reinterpret_cast<Vec<uint64_t, V>*>(p) = o;
+    }
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // Persistent variant: a grid of about one wave strides over the neuron tiles, and each warp loads the
 // tables of its next tile while the operand words of the current one are in flight, so a tile costs one
 // memory round trip instead of two (tables, then operands) plus a CTA launch.
-template <int R, int V, int MINB = 1>
+template <int R, int V, int MINB = 1, int ST = 0>
 __global__ void __launch_bounds__(256, MINB)
 packed_layer_pipe_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nwords, const int2* __restrict__ sel_ab,
                          const uint8_t* __restrict__ sel_gate, int64_t n_out, uint64_t* __restrict__ y, int64_t ldy,
@@ -263,6 +306,7 @@ packed_layer_pipe_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nw
     const int64_t stride = (((int64_t)gridDim.y * blockDim.x) >> 5) * npw * R;
     pdl_trigger();
     if (w >= nwords) return;
+    const uint64_t policy = ST ? evict_first_policy() : 0ull;
     const int64_t sub = lane >> tw_log2;
     int64_t base = warp_global * npw * R;
     int2 ab[R];
@@ -298,7 +342,7 @@ packed_layer_pipe_kernel(const uint64_t* __restrict__ x, int64_t ldx, int64_t nw
                 Vw o;
 #pragma unroll
                 for (int i = 0; i < V; ++i) o.v[i] = gate_word<uint64_t>(gc[q], va[q].v[i], vb[q].v[i]);
-                *reinterpret_cast<Vw*>(y + j * ldy + w) = o;
+                store_words<ST, V>(y + j * ldy + w, o, policy);
             }
         }
     }
@@ -367,33 +411,15 @@ struct CountPlan {
     int64_t groups;   // CTAs per (class, column tile) = ceil(nseg / S)
 };
 
+// CTA fold of the per-thread counters: each thread's 64 counts go to shared memory as four 16-bit lanes
+// per word, the S segments of each (column, 4-position group) are summed (packed 16-bit adds cannot
+// overflow: at most 256 * 240 < 65536 per lane), and each total goes to global memory once.
 // partial != null: instead of atomics into counts, the CTA stores its totals (zeros included) to
 // partial[blockIdx.y][64 * w + pos] (row length 64 * gridDim.x * TW) and sum_partials folds them.
-template <class Src>
-__global__ void __launch_bounds__(256)
-count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int64_t k, const int64_t class_size,
-             const CountPlan plan, int32_t* __restrict__ counts, const int64_t sample0, const int64_t samples,
-             int32_t* __restrict__ partial) {
-    // [thread][position / 4]: each thread's 64 counts as four 16-bit lanes per word, no atomics
-    __shared__ unsigned long long s_cnt[256 * 16];
-    const int TW = 1 << plan.tw_log2;
-    const int S = 256 >> plan.tw_log2;
-    const int wl = threadIdx.x & (TW - 1), sl = threadIdx.x >> plan.tw_log2;
-    const int64_t c = blockIdx.y / plan.groups;
-    const int64_t seg = (blockIdx.y - c * plan.groups) * S + sl;
-    const int64_t w = (int64_t)blockIdx.x * TW + wl;
-    pdl_trigger();
-    pdl_wait();
-    VCounter vc;
-    if (w < nwords && seg < plan.nseg) {
-        const int64_t r0 = c * class_size + seg * plan.seg_len;
-        const int64_t r1 = min(min(r0 + plan.seg_len, (c + 1) * class_size), rows);
-        for (int64_t r = r0; r < r1; r += 16) {
-            uint64_t d[16];
-            src.load16(r, r1, w, d);
-            vc.add16(d);
-        }
-    }
+__device__ __forceinline__ void count_fold(const VCounter& vc, unsigned long long* s_cnt, const int TW, const int S,
+                                           const int64_t nwords, const int64_t k, const int64_t c,
+                                           int32_t* __restrict__ counts, const int64_t sample0, const int64_t samples,
+                                           int32_t* __restrict__ partial) {
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
         const uint64_t v8 = vc.counts8(m);
@@ -408,8 +434,6 @@ count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int6
         s_cnt[threadIdx.x * 16 + ((2 * m + 1 + threadIdx.x) & 15)] = hi;
     }
     __syncthreads();
-    // fold the S segments of each (column, 4-position group): packed 16-bit adds cannot overflow
-    // (at most 256 * 240 < 65536 per lane)
     for (int e = threadIdx.x; e < TW * 16; e += blockDim.x) {
         const int col = e >> 4, grp = e & 15;
         unsigned long long acc = 0;
@@ -429,6 +453,93 @@ count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int6
                 atomicAdd(counts + (sample0 + n) * k + c, v);
         }
     }
+}
+
+template <class Src>
+__global__ void __launch_bounds__(256)
+count_kernel(const Src src, const int64_t rows, const int64_t nwords, const int64_t k, const int64_t class_size,
+             const CountPlan plan, int32_t* __restrict__ counts, const int64_t sample0, const int64_t samples,
+             int32_t* __restrict__ partial) {
+    __shared__ unsigned long long s_cnt[256 * 16];  // [thread][position / 4]
+    const int TW = 1 << plan.tw_log2;
+    const int S = 256 >> plan.tw_log2;
+    const int wl = threadIdx.x & (TW - 1), sl = threadIdx.x >> plan.tw_log2;
+    const int64_t c = blockIdx.y / plan.groups;
+    const int64_t seg = (blockIdx.y - c * plan.groups) * S + sl;
+    const int64_t w = (int64_t)blockIdx.x * TW + wl;
+    pdl_trigger();
+    pdl_wait();
+    VCounter vc;
+    if (w < nwords && seg < plan.nseg) {
+        const int64_t r0 = c * class_size + seg * plan.seg_len;
+        const int64_t r1 = min(min(r0 + plan.seg_len, (c + 1) * class_size), rows);
+        for (int64_t r = r0; r < r1; r += 16) {
+            uint64_t d[16];
+            src.load16(r, r1, w, d);
+            vc.add16(d);
+        }
+    }
+    count_fold(vc, s_cnt, TW, S, nwords, k, c, counts, sample0, samples, partial);
+}
+
+// The fused last layer as a software pipeline over groups of 8 neurons: the tables (operand rows, gate)
+// of the next group are loaded while the 16 operand words of the current group are in flight, so a
+// group costs one memory round trip instead of two (tables, then operands), with about half the
+// registers of count_kernel<GateWords> (more resident warps).  The tables do not depend on the
+// previous layer, so the first group's are loaded before the programmatic-launch wait.
+template <int MINB>
+__global__ void __launch_bounds__(256, MINB)
+count_gate_pipe_kernel(const GateWords src, const int64_t rows, const int64_t nwords, const int64_t k,
+                       const int64_t class_size, const CountPlan plan, int32_t* __restrict__ counts,
+                       const int64_t sample0, const int64_t samples, int32_t* __restrict__ partial) {
+    __shared__ unsigned long long s_cnt[256 * 16];
+    const int TW = 1 << plan.tw_log2;
+    const int S = 256 >> plan.tw_log2;
+    const int wl = threadIdx.x & (TW - 1), sl = threadIdx.x >> plan.tw_log2;
+    const int64_t c = blockIdx.y / plan.groups;
+    const int64_t seg = (blockIdx.y - c * plan.groups) * S + sl;
+    const int64_t w = (int64_t)blockIdx.x * TW + wl;
+    pdl_trigger();
+    VCounter vc;
+    const bool active = w < nwords && seg < plan.nseg;
+    int64_t r0 = 0, r1 = 0;
+    int2 p[8];
+    int g[8];
+    if (active) {
+        r0 = c * class_size + seg * plan.seg_len;
+        r1 = min(min(r0 + plan.seg_len, (c + 1) * class_size), rows);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int64_t jj = min(r0 + q, r1 - 1);
+            p[q] = src.ab[jj];
+            g[q] = src.gate[jj];
+        }
+    }
+    pdl_wait();  // the operand rows are the previous layer's output
+    if (active) {
+        const uint64_t* __restrict__ xw = src.x + w;
+        for (int64_t r = r0; r < r1; r += 8) {
+            uint64_t va[8], vb[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                va[q] = p[q].x >= 0 ? __ldg(xw + (int64_t)p[q].x * src.ldx) : 0ull;
+                vb[q] = p[q].y >= 0 ? __ldg(xw + (int64_t)p[q].y * src.ldx) : 0ull;
+            }
+            int gc[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                gc[q] = g[q];
+                const int64_t jj = min(r + 8 + q, r1 - 1);
+                p[q] = src.ab[jj];
+                g[q] = src.gate[jj];
+            }
+            uint64_t d[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) d[q] = (r + q < r1) ? gate_word<uint64_t>(gc[q], va[q], vb[q]) : 0ull;
+            vc.add8(d);
+        }
+    }
+    count_fold(vc, s_cnt, TW, S, nwords, k, c, counts, sample0, samples, partial);
 }
 
 // counts[(sample0 + n) * k + c] += sum_g partial[c * groups + g][n]   (one writer per element)
@@ -495,6 +606,34 @@ CountPlan plan_count(int64_t k, int64_t class_size, int64_t W, bool to_partial) 
 }
 
 template <class Src>
+void launch_count_kernel(const Src& src, dim3 grid, cudaStream_t s, int64_t rows, int64_t nwords, int64_t k,
+                         int64_t class_size, const CountPlan& p, int32_t* counts, int64_t sample0, int64_t samples,
+                         int32_t* partial) {
+    launch_chain(count_kernel<Src>, grid, dim3(256), s, src, rows, nwords, k, class_size, p, counts, sample0, samples,
+                 partial);
+}
+
+// The fused last layer: the pipelined kernel by default; CLB_COUNT_PIPE=0 selects count_kernel<GateWords>,
+// CLB_COUNT_PIPE=2 the pipelined kernel with its registers capped for 3 resident CTAs per SM.
+void launch_count_kernel(const GateWords& src, dim3 grid, cudaStream_t s, int64_t rows, int64_t nwords, int64_t k,
+                         int64_t class_size, const CountPlan& p, int32_t* counts, int64_t sample0, int64_t samples,
+                         int32_t* partial) {
+    static const int mode = [] {
+        const char* e = getenv("CLB_COUNT_PIPE");
+        return e != nullptr ? atoi(e) : 1;
+    }();
+    if (mode == 0)
+        launch_chain(count_kernel<GateWords>, grid, dim3(256), s, src, rows, nwords, k, class_size, p, counts, sample0,
+                     samples, partial);
+    else if (mode == 2)
+        launch_chain(count_gate_pipe_kernel<3>, grid, dim3(256), s, src, rows, nwords, k, class_size, p, counts,
+                     sample0, samples, partial);
+    else
+        launch_chain(count_gate_pipe_kernel<2>, grid, dim3(256), s, src, rows, nwords, k, class_size, p, counts,
+                     sample0, samples, partial);
+}
+
+template <class Src>
 cudaError_t launch_count(const Src& src, int64_t rows, int64_t nwords, int64_t k, int64_t class_size,
                          int32_t* counts, int64_t sample0, int64_t samples, void* ws, size_t ws_bytes,
                          cudaStream_t s) {
@@ -511,8 +650,7 @@ cudaError_t launch_count(const Src& src, int64_t rows, int64_t nwords, int64_t k
     }
     if (k * p.groups > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)tiles, (unsigned)(k * p.groups));
-    launch_chain(count_kernel<Src>, grid, dim3(256), s, src, rows, nwords, k, class_size, p, counts, sample0, samples,
-                 partial);
+    launch_count_kernel(src, grid, s, rows, nwords, k, class_size, p, counts, sample0, samples, partial);
     if (partial != nullptr) {
         launch_chain(sum_partials_kernel, dim3(grid_for(samples * k)), dim3(256), s, (const int32_t*)partial, row,
                      p.groups, k, counts, sample0, samples);
@@ -596,7 +734,11 @@ void packed_layer_go(dim3 grid, cudaStream_t s, int minb, const uint64_t* x, int
         // about `pipe` waves of resident CTAs, striding over the tiles
         const int64_t cap = std::max<int64_t>(1, (int64_t)sm_count() * (minb == 4 ? 4 : 2) * pipe / grid.x);
         grid.y = (unsigned)std::min<int64_t>(grid.y, cap);
-        if (minb == 4)
+        static const int st = packed_env("CLB_PACKED_ST", 1);  // evict-first stores (measured 400.6 -> 398.2 ms per c4 pass)
+        if (minb == 4 && st == 1)
+            launch_chain(packed_layer_pipe_kernel<R, V, 4, 1>, grid, dim3(256), s, x, ldx, nwords, ab, g, n_out, y,
+                         ldy, tw_log2);
+        else if (minb == 4)
             launch_chain(packed_layer_pipe_kernel<R, V, 4>, grid, dim3(256), s, x, ldx, nwords, ab, g, n_out, y, ldy,
                          tw_log2);
         else
