@@ -2,7 +2,7 @@
 //
 // The scatter backward (logic_layer.cu) walks slots and adds each slot's activation gradient into
 // grad_x with L2 reductions.  Here the work is walked by destination instead: a per-layer index lists,
-// for every input feature i, the slot operands that read it ("occurrences", sorted by slot, so the
+// for every input feature i, the slot operands that read it ("occurrences", sorted owners first, then by slot, so the
 // summation order is fixed for a given index).  One warp owns one input row and one column chunk;
 // for each occurrence it gathers the other operand's row and grad_y of the slot's neuron, and
 //   grad_x[i, n]        += p * (c_self + c3 * x_other) * gy[j, n]       (difflogic_kernel.cu:140-194)
@@ -143,7 +143,12 @@ __global__ void index_fill_kernel(const int2* slots, const uint8_t* gates, int64
     for (int i = 0; i < n; ++i) tmp[atomicAdd(cursor + row[i], 1)] = rec[i];
 }
 
-// Order each row's occurrences by record key (unique per slot and side): rank sort, one warp per row.
+// Sort key of a record: owners (bit 5 of meta) first, then by meta (unique per slot and side).
+__device__ __forceinline__ uint64_t occ_key(int meta) {
+    return ((uint64_t)(((meta >> 5) & 1) ^ 1) << 32) | (uint32_t)meta;
+}
+
+// Order each row's occurrences by record key, owners first: rank sort, one warp per row.
 __global__ void index_sort_kernel(const int32_t* starts, int64_t in_features, const int2* tmp, int2* recs) {
     const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -151,9 +156,9 @@ __global__ void index_sort_kernel(const int32_t* starts, int64_t in_features, co
     const int beg = starts[row], end = starts[row + 1];
     for (int e = beg + lane; e < end; e += 32) {
         const int2 r = tmp[e];
-        const uint32_t key = (uint32_t)r.y;
+        const uint64_t key = occ_key(r.y);
         int rank = 0;
-        for (int q = beg; q < end; ++q) rank += (uint32_t)tmp[q].y < key;
+        for (int q = beg; q < end; ++q) rank += occ_key(tmp[q].y) < key;
         recs[beg + rank] = r;
     }
 }
@@ -225,6 +230,7 @@ struct GatherArgs {
     int64_t n_out;
     int K;
     int64_t group;
+    int split;  // gather2: light loop for non-owner occurrences (CLB_GATHER_SPLIT=0 turns it off)
 };
 
 // Gate coefficients of one occurrence, from the point of view of its own operand ("s", the row the
@@ -407,17 +413,25 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
     for (int base = beg; base < end; base += 32) {
         const int n = min(32, end - base);
         __syncwarp();
+        const int my_slot = lane < n ? owner_slot[base + lane] : -1;
         if (lane < n) {
             srec[warp][2 * lane] = baked[2 * (base + lane)];
             srec[warp][2 * lane + 1] = baked[2 * (base + lane) + 1];
-            sslot[warp][lane] = owner_slot[base + lane];
         } else {  // zero records: own row, coefficient 0, no owner
             srec[warp][2 * lane] = make_int4(-1, 0, 0, 0);
             srec[warp][2 * lane + 1] = make_int4(0, 0, 0, 0);
-            sslot[warp][lane] = -1;
         }
+        sslot[warp][lane] = my_slot;
+        // The index lists a row's owner occurrences first, so the owners of this batch are a prefix of it:
+        // only they need the gate value, the d loss / d p reduction and its store.  The rest (the second
+        // operand of two-operand slots) take the light loop below.  Not a prefix: the whole batch is full.
+        const unsigned om = __ballot_sync(0xffffffffu, my_slot >= 0);
+        const int nown = __popc(om);
+        const int split = part == nullptr ? 0
+                          : a.split && om == (nown == 32 ? 0xffffffffu : (1u << nown) - 1u) ? min(n, (nown + kU2 - 1) / kU2 * kU2)
+                                                                                  : n;
         __syncwarp();
-        for (int e = 0; e < n; e += kU2) {
+        for (int e = 0; e < split; e += kU2) {
             float xo[kU2][4];
             float4 g[kU2];
             int4 r[kU2];
@@ -449,6 +463,25 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
                 constexpr int SH = kU2 == 8 ? 2 : kU2 == 4 ? 3 : 4;  // log2(lanes per reduced value) = 5 - log2(kU2)
                 const int slot = sslot[warp][(e + ((lane >> SH) & (kU2 - 1))) & 31];
                 if ((lane & ((1 << SH) - 1)) == 0 && slot >= 0) part[pbase + slot] = dot[0];
+            }
+        }
+        // light loop: grad_x only (records past n are zero records)
+        for (int e = split; e < n; e += kU2) {
+            float xo[kU2][4];
+            float4 g[kU2];
+            int4 r[kU2];
+#pragma unroll
+            for (int u = 0; u < kU2; ++u) {
+                r[u] = srec[warp][2 * ((e + u) & 31)];
+                load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
+                g[u] = *reinterpret_cast<const float4*>(gsrc + r[u].y + lcol);
+            }
+#pragma unroll
+            for (int u = 0; u < kU2; ++u) {
+                const float pcs = __int_as_float(r[u].z), pc3 = __int_as_float(r[u].w);
+                const float gg[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[i] = fmaf(fmaf(pc3, xo[u][i], pcs), gg[i], acc[i]);
             }
         }
     }
@@ -553,11 +586,17 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
             return (v == 43 || v == 25 || v == 26) ? v : 44;
         }();
         int* owner = reinterpret_cast<int*>(a.tmp);
+        static const int split = [] {
+            const char* e = getenv("CLB_GATHER_SPLIT");
+            return (e && e[0] == '0') ? 0 : 1;
+        }();
+        GatherArgs as = a;
+        as.split = split;
         switch (cfg) {
-            case 43: logic_backward_gather2_kernel<T, 4, 3><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
-            case 25: logic_backward_gather2_kernel<T, 2, 5><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
-            case 26: logic_backward_gather2_kernel<T, 2, 6><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
-            default: logic_backward_gather2_kernel<T, 4, 4><<<grid, kThreads, 0, s>>>(a, a.baked, owner); break;
+            case 43: logic_backward_gather2_kernel<T, 4, 3><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
+            case 25: logic_backward_gather2_kernel<T, 2, 5><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
+            case 26: logic_backward_gather2_kernel<T, 2, 6><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
+            default: logic_backward_gather2_kernel<T, 4, 4><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
         }
         return cudaGetLastError();
     }
