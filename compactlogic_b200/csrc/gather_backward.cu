@@ -489,6 +489,124 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
         make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
 
+// The 4 pieces (columns p + 32 m .. p + 32 m + 3, m = 0..3) of a gather4 lane's share of a row.
+template <typename T>
+__device__ __forceinline__ void load_pieces(const T* __restrict__ p, float (&out)[16]) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        float v[4];
+        load_acc<T, 4>(p + 32 * m, v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) out[4 * m + i] = v[i];
+    }
+}
+
+// Variant of logic_backward_gather2_kernel with 8 lanes per occurrence: lane (q, c) = (lane / 8, lane % 8)
+// owns columns 32 m + 4 c .. 32 m + 4 c + 3 (m = 0..3) of the 128-column chunk, so each 4-column load of
+// a quarter-warp is one contiguous 128-byte piece of a row, and works on occurrence e + q, so one warp step
+// covers 4 occurrences.  A 128-bit shared-memory read then fetches 4 different records (one per
+// quarter-warp) instead of broadcasting one record to all 32 lanes (several wavefronts for one record),
+// the gate-value dot product is reduced over 8 lanes (3 shuffles per 4 occurrences instead of a 6-shuffle
+// butterfly), and the 4 partial grad_x rows are summed once per row by a 2-step reduce-scatter at the
+// end.  Row gathers stay 512 bytes per occurrence (8 lanes x 4 pieces of 16 bytes).  Needs ncols % 128 == 0.
+template <typename T, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather4_kernel(
+    const GatherArgs a, const int4* __restrict__ baked, const int* __restrict__ owner_slot) {
+    constexpr int C = 16;  // columns per lane
+    __shared__ int4 srec[kWarps][2 * 32];
+    __shared__ int sslot[kWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int q = lane >> 3, cg = lane & 7;
+    const int row = blockIdx.x * kWarps + warp;
+    if (row >= (int)a.in_features) return;
+    const int chunk = blockIdx.y;
+    const int lcol = chunk * 128 + cg * 4;  // + 32 m for piece m; every column is < ncols
+    const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
+    const float* __restrict__ gsrc = reinterpret_cast<const float*>(a.gs_grad != nullptr ? a.gs_grad : a.gy);
+    const int rowoff = row * (int)a.ldx;
+    float* part = reinterpret_cast<float*>(a.part);
+    const int64_t pbase = (int64_t)chunk * a.n_out * a.K;
+    float xs[C];
+    load_pieces<T>(x + rowoff + lcol, xs);
+    float acc[C];
+#pragma unroll
+    for (int i = 0; i < C; ++i) acc[i] = 0.f;
+    const int beg = a.starts[row], end = a.starts[row + 1];
+    for (int base = beg; base < end; base += 32) {
+        const int n = min(32, end - base);
+        __syncwarp();
+        const int my_slot = lane < n ? owner_slot[base + lane] : -1;
+        if (lane < n) {
+            srec[warp][2 * lane] = baked[2 * (base + lane)];
+            srec[warp][2 * lane + 1] = baked[2 * (base + lane) + 1];
+        } else {  // zero records: own row, coefficient 0, no owner
+            srec[warp][2 * lane] = make_int4(-1, 0, 0, 0);
+            srec[warp][2 * lane + 1] = make_int4(0, 0, 0, 0);
+        }
+        sslot[warp][lane] = my_slot;
+        // owners first (see gather2): they need the gate value and its reduction, the rest only grad_x
+        const unsigned om = __ballot_sync(0xffffffffu, my_slot >= 0);
+        const int nown = __popc(om);
+        const int split = part == nullptr ? 0
+                          : a.split && om == (nown == 32 ? 0xffffffffu : (1u << nown) - 1u)
+                              ? min(n, (nown + 3) & ~3)
+                              : n;
+        __syncwarp();
+        for (int e = 0; e < split; e += 4) {
+            const int o = (e + q) & 31;
+            const int4 r = srec[warp][2 * o];
+            float xo[C], g[C];
+            load_pieces<T>(x + (r.x >= 0 ? r.x : rowoff) + lcol, xo);
+            load_pieces<float>(gsrc + r.y + lcol, g);
+            const int4 cd = srec[warp][2 * o + 1];
+            const float pcs = __int_as_float(r.z), pc3 = __int_as_float(r.w);
+            const float c0 = __int_as_float(cd.x), cs = __int_as_float(cd.y), co = __int_as_float(cd.z),
+                        c3 = __int_as_float(cd.w);
+            float d = 0.f;
+#pragma unroll
+            for (int i = 0; i < C; ++i) {
+                acc[i] = fmaf(fmaf(pc3, xo[i], pcs), g[i], acc[i]);
+                d = fmaf(g[i], fmaf(fmaf(c3, xs[i], co), xo[i], fmaf(cs, xs[i], c0)), d);
+            }
+            d += __shfl_xor_sync(0xffffffffu, d, 4);
+            d += __shfl_xor_sync(0xffffffffu, d, 2);
+            d += __shfl_xor_sync(0xffffffffu, d, 1);
+            if (part != nullptr && cg == 0) {
+                const int slot = sslot[warp][o];
+                if (slot >= 0) part[pbase + slot] = d;
+            }
+        }
+        for (int e = split; e < n; e += 4) {  // non-owners: grad_x only (records past n are zero records)
+            const int4 r = srec[warp][2 * ((e + q) & 31)];
+            float xo[C], g[C];
+            load_pieces<T>(x + (r.x >= 0 ? r.x : rowoff) + lcol, xo);
+            load_pieces<float>(gsrc + r.y + lcol, g);
+            const float pcs = __int_as_float(r.z), pc3 = __int_as_float(r.w);
+#pragma unroll
+            for (int i = 0; i < C; ++i) acc[i] = fmaf(fmaf(pc3, xo[i], pcs), g[i], acc[i]);
+        }
+    }
+    // sum the 4 occurrence groups' rows: after the two steps lane (q, c) holds the total of piece m = q
+    {
+        const bool up = (lane & 16) != 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float send = up ? acc[i] : acc[i + 8];
+            const float keep = up ? acc[i + 8] : acc[i];
+            acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+        const bool up2 = (lane & 8) != 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float send = up2 ? acc[i] : acc[i + 4];
+            const float keep = up2 ? acc[i + 4] : acc[i];
+            acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+    }
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.gx) + (int64_t)row * a.ldgx + lcol + 32 * q) =
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
 // The fast (baked) path applies to fp32 / bf16 / fp16 activations with whole 4-column vectors and every element offset below 2^31.
 bool fast_ok(const GatherArgs& a) {
     static const bool enabled = [] {
@@ -592,6 +710,21 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
         }();
         GatherArgs as = a;
         as.split = split;
+        // CLB_GATHER4: 0 = gather2, 3 / 2 = the 8-lanes-per-occurrence kernel with 3 / 2 resident CTAs per SM;
+        // unset = gather4 (3) for fp32 layers averaging >= 64 occurrences per input row, where its per-row
+        // reduce-scatter is amortised (measured: c3 dense layer 0.87 -> 0.79 ms; c2, 32 per row, 1.08 ->
+        // 1.24 ms, and bf16 rows, whose 8-byte pieces half-fill a quarter-warp's 128 bytes, slower)
+        static const int g4env = [] {
+            const char* e = getenv("CLB_GATHER4");
+            return e ? atoi(e) : -1;
+        }();
+        const bool dense_rows = std::is_same<T, float>::value && 2 * a.n_out * a.K >= 64 * a.in_features;
+        const int g4 = g4env >= 0 ? g4env : (dense_rows ? 3 : 0);
+        if (g4 != 0 && a.ncols % 128 == 0) {
+            if (g4 == 2) logic_backward_gather4_kernel<T, 2><<<grid, kThreads, 0, s>>>(as, a.baked, owner);
+            else logic_backward_gather4_kernel<T, 3><<<grid, kThreads, 0, s>>>(as, a.baked, owner);
+            return cudaGetLastError();
+        }
         switch (cfg) {
             case 43: logic_backward_gather2_kernel<T, 4, 3><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
             case 25: logic_backward_gather2_kernel<T, 2, 5><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
