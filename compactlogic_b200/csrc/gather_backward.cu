@@ -387,7 +387,26 @@ __global__ void bake_kernel(const int2* __restrict__ recs, const int32_t* __rest
     owner_slot[e] = owner ? (int)slot : -1;
 }
 
-template <typename T, int kU2, int MINB>  // activation type, occurrences in flight per warp step, CTAs per SM
+// Broadcast read of a staged 16-byte record as one 128-bit, two 64-bit or four 32-bit shared loads.
+template <int LDW>
+__device__ __forceinline__ int4 lds_rec(const int4* p) {
+    const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+    int4 r;
+    if constexpr (LDW == 2) {  // inline PTX so the two halves are not fused into one 128-bit load
+        asm volatile("ld.shared.v2.s32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
+        asm volatile("ld.shared.v2.s32 {%0, %1}, [%2];" : "=r"(r.z), "=r"(r.w) : "r"(a + 8));
+    } else if constexpr (LDW == 4) {
+        asm volatile("ld.shared.s32 %0, [%1];" : "=r"(r.x) : "r"(a));
+        asm volatile("ld.shared.s32 %0, [%1];" : "=r"(r.y) : "r"(a + 4));
+        asm volatile("ld.shared.s32 %0, [%1];" : "=r"(r.z) : "r"(a + 8));
+        asm volatile("ld.shared.s32 %0, [%1];" : "=r"(r.w) : "r"(a + 12));
+    } else {
+        r = *p;
+    }
+    return r;
+}
+
+template <typename T, int kU2, int MINB, int LDW = 1>  // activation type, occurrences in flight per warp step, CTAs per SM, record read width
 __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
     const GatherArgs a, const int4* __restrict__ baked, const int* __restrict__ owner_slot) {
     __shared__ int4 srec[kWarps][2 * 32];
@@ -437,14 +456,14 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
             int4 r[kU2];
 #pragma unroll
             for (int u = 0; u < kU2; ++u) {
-                r[u] = srec[warp][2 * ((e + u) & 31)];
+                r[u] = lds_rec<LDW>(&srec[warp][2 * ((e + u) & 31)]);
                 load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
                 g[u] = *reinterpret_cast<const float4*>(gsrc + r[u].y + lcol);
             }
             float dot[kU2];
 #pragma unroll
             for (int u = 0; u < kU2; ++u) {
-                const int4 cd = srec[warp][2 * ((e + u) & 31) + 1];
+                const int4 cd = lds_rec<LDW>(&srec[warp][2 * ((e + u) & 31) + 1]);
                 const float pcs = __int_as_float(r[u].z), pc3 = __int_as_float(r[u].w);
                 const float c0 = __int_as_float(cd.x), cs = __int_as_float(cd.y), co = __int_as_float(cd.z),
                             c3 = __int_as_float(cd.w);
@@ -472,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
             int4 r[kU2];
 #pragma unroll
             for (int u = 0; u < kU2; ++u) {
-                r[u] = srec[warp][2 * ((e + u) & 31)];
+                r[u] = lds_rec<LDW>(&srec[warp][2 * ((e + u) & 31)]);
                 load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
                 g[u] = *reinterpret_cast<const float4*>(gsrc + r[u].y + lcol);
             }
@@ -697,11 +716,13 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
         }
         dim3 grid((unsigned)ceil_div64(a.in_features, kWarps), (unsigned)ceil_div64(a.ncols, 128));
         if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-        // CLB_GATHER2: occurrences in flight x resident CTAs per SM (tuning; 44 = 4 x 4, the default)
+        // CLB_GATHER2: occurrences in flight x resident CTAs per SM (tuning; 44 = 4 x 4, the default), with the
+        // staged records read as four 32-bit broadcasts (one shared wavefront each; a 128-bit broadcast costs
+        // several: c2 gather 1.082 -> 1.069 ms); 441 / 442 read them as one 128-bit / two 64-bit loads
         static const int cfg = [] {
             const char* e = getenv("CLB_GATHER2");
             const int v = e ? atoi(e) : 44;
-            return (v == 43 || v == 25 || v == 26) ? v : 44;
+            return (v == 43 || v == 25 || v == 26 || v == 441 || v == 442) ? v : 44;
         }();
         int* owner = reinterpret_cast<int*>(a.tmp);
         static const int split = [] {
@@ -729,7 +750,9 @@ cudaError_t gather_t(const GatherArgs& a, int mode, const void* weights, cudaStr
             case 43: logic_backward_gather2_kernel<T, 4, 3><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
             case 25: logic_backward_gather2_kernel<T, 2, 5><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
             case 26: logic_backward_gather2_kernel<T, 2, 6><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
-            default: logic_backward_gather2_kernel<T, 4, 4><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
+            case 441: logic_backward_gather2_kernel<T, 4, 4, 1><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
+            case 442: logic_backward_gather2_kernel<T, 4, 4, 2><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
+            default: logic_backward_gather2_kernel<T, 4, 4, 4><<<grid, kThreads, 0, s>>>(as, a.baked, owner); break;
         }
         return cudaGetLastError();
     }
