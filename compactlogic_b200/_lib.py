@@ -49,6 +49,9 @@ _SIGS = {
     "clb_slots_conv": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p, _p, _p]),
     "clb_logic_forward": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _p, _int, _p, _i64, _p,
                                  _i64, _i64, _i64, _p]),
+    "clb_logic_forward_stage_bytes": (_sz, [_int, _i64, _i64]),
+    "clb_logic_forward_staged": (_int, [_int, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _p, _int, _p,
+                                        _i64, _p, _i64, _i64, _i64, _p, _sz, _p]),
     "clb_logic_backward_chunks": (_i64, [_int, _p, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64]),
     "clb_logic_backward": (_int, [_int, _p, _i64, _i64, _p, _i64, _i64, _i64, _int, _p, _p, _int, _p, _i64, _p, _i64,
                                   _i64, _i64, _dbl, _p, _i64, _int, _i64, _p, _i64, _p]),

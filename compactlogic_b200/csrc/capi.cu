@@ -130,11 +130,30 @@ int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, int6
                       int64_t K, int64_t group, int weight_mode, const void* weights, const uint8_t* gates,
                       const uint8_t* select, int has_pad, void* y, int64_t ldy, void* gs_acc, int64_t gs_k,
                       int64_t gs_size, int64_t ld_gs, clb_stream_t stream) {
+    return clb_logic_forward_staged(dtype, x, ldx, ncols, in_features, slots, n_out, K, group, weight_mode, weights,
+                                    gates, select, has_pad, y, ldy, gs_acc, gs_k, gs_size, ld_gs, nullptr, 0, stream);
+}
+
+size_t clb_logic_forward_stage_bytes(int dtype, int64_t n_out, int64_t K) {
+    if (n_out < 1 || K < 1) return 0;
+    return logic_forward_stage_bytes(dtype, n_out, K);
+}
+
+int clb_logic_forward_staged(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
+                             const int32_t* slots, int64_t n_out, int64_t K, int64_t group, int weight_mode,
+                             const void* weights, const uint8_t* gates, const uint8_t* select, int has_pad, void* y,
+                             int64_t ldy, void* gs_acc, int64_t gs_k, int64_t gs_size, int64_t ld_gs, void* stage,
+                             size_t stage_bytes, clb_stream_t stream) {
     int st = check_layer(dtype, n_out, K, group, weight_mode, weights, gates, select, slots);
     if (st) return st;
     if (ncols < 0 || ldx < ncols) return fail(CLB_ERR_INVALID, "forward: ldx %lld < ncols %lld", (long long)ldx, (long long)ncols);
     if (ncols == 0 || n_out == 0) return CLB_OK;
     if (!x) return fail(CLB_ERR_INVALID, "forward: null x");
+    if (stage != nullptr) {
+        const size_t need = logic_forward_stage_bytes(dtype, n_out, K);
+        if (stage_bytes < need || (uintptr_t)stage % 256 != 0)
+            return fail(CLB_ERR_WORKSPACE, "forward: stage of %zu bytes (256-aligned) needed, got %zu", need, stage_bytes);
+    }
     GroupSumArgs gs{};
     if (gs_acc) {
         if (gs_k < 1 || gs_size < 1 || ld_gs < ncols || gs_k * gs_size < n_out)
@@ -148,7 +167,8 @@ int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, int6
     }
     const LayerArgs a = layer(dtype, x, ldx, ncols, slots, n_out, K, group, weight_mode, weights, gates, select, has_pad,
                               in_features);
-    return cuda_status(launch_logic_forward(a, y, ldy, gs_acc ? &gs : nullptr, S(stream)), "logic_forward");
+    return cuda_status(launch_logic_forward(a, y, ldy, gs_acc ? &gs : nullptr, S(stream), nullptr, stage),
+                       "logic_forward_staged");
 }
 
 int64_t clb_logic_backward_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,

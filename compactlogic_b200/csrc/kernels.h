@@ -50,8 +50,11 @@ struct GroupSumArgs {
     double scale;      // backward: grad_y[j, col] = grad[class(j), col] * scale
 };
 
+// stage != null: the forward stage is baked once into that buffer (logic_forward_stage_bytes bytes)
+// instead of being rebuilt by every CTA of every column chunk.
 cudaError_t launch_logic_forward(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs,
-                                 cudaStream_t s, const PeerArgs* peers = nullptr);
+                                 cudaStream_t s, const PeerArgs* peers = nullptr, void* stage = nullptr);
+size_t logic_forward_stage_bytes(int dtype, int64_t n_out, int64_t K);
 
 // Fused backward: reads x once per slot and produces both the per-chunk partial sums of
 // d loss / d prob (when `partials` != null) and the scattered activation gradient (when gx != null,

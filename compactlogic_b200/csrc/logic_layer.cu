@@ -281,23 +281,89 @@ __device__ __forceinline__ void gather_off(const T* __restrict__ xc, int off, ty
     load_acc<T, VEC>(p, v);
 }
 
+// Forward stage baked once per call: the softmax, the compaction into two- / one-operand entries and
+// (offset mode) the row-offset scaling depend only on the neuron, yet the stage is otherwise rebuilt by
+// every CTA of every column chunk.  fwd_bake_kernel writes it once to global memory ([nb, K] entries,
+// nb = n_out rounded up to TN), and the forward CTAs copy their TN neurons' part into shared memory.
+template <typename A> struct FwdBake {
+    A4<A>* cf;
+    int2* ab;
+    A* c0;
+    int* ns;
+    int* n1;
+};
+
+inline size_t r256(size_t v) { return (v + 255) & ~size_t(255); }
+
+template <typename A>
+size_t bake_bytes(int64_t nb, int K) {
+    return r256((size_t)nb * K * sizeof(A4<A>)) + r256((size_t)nb * K * sizeof(int2)) + r256((size_t)nb * sizeof(A)) +
+           2 * r256((size_t)nb * sizeof(int));
+}
+
+template <typename A>
+FwdBake<A> carve_bake(void* base, int64_t nb, int K) {
+    unsigned char* b = reinterpret_cast<unsigned char*>(base);
+    FwdBake<A> f;
+    f.cf = reinterpret_cast<A4<A>*>(b);
+    b += r256((size_t)nb * K * sizeof(A4<A>));
+    f.ab = reinterpret_cast<int2*>(b);
+    b += r256((size_t)nb * K * sizeof(int2));
+    f.c0 = reinterpret_cast<A*>(b);
+    b += r256((size_t)nb * sizeof(A));
+    f.ns = reinterpret_cast<int*>(b);
+    b += r256((size_t)nb * sizeof(int));
+    f.n1 = reinterpret_cast<int*>(b);
+    return f;
+}
+
+template <typename A, bool OFF>
+__global__ void __launch_bounds__(kThreads) fwd_bake_kernel(const LayerArgs a, const int TN, const FwdBake<A> f) {
+    const int K = a.K;
+    const int64_t j0 = (int64_t)blockIdx.x * TN;
+    Stage<A> st;
+    st.cf = f.cf + j0 * K;
+    st.ab = f.ab + j0 * K;
+    st.p = nullptr;
+    st.c0 = f.c0 + j0;
+    st.ns = f.ns + j0;
+    st.n1 = f.n1 + j0;
+    fill_stage<A, false>(a, j0, TN, st);
+    if (OFF) scale_stage(st.ab, TN * K, a.ldx);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Forward: y[j, n] = sum_k p[r,k] * f_{g[r,k]}(x[a_jk, n], x[b_jk, n])   (difflogic_kernel.cu:39-78)
 // Select mode (float eval, difflogic_kernel.cu:341-369): only the chosen slot, p = 1.
 // With GroupSum fused (compactlogic.py:460-465), y is never written; per-class column sums are
 // accumulated into gs.acc instead.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int VEC, bool PEERS, bool OFF>
+template <typename T, int VEC, bool PEERS, bool OFF, bool BAKED = false>
 __global__ void __launch_bounds__(kThreads)
 logic_forward_kernel(const LayerArgs a, T* __restrict__ y, const int64_t ldy, const GroupSumArgs gs,
-                     const bool use_gs, const int TN, const PeerArgs pa) {
+                     const bool use_gs, const int TN, const PeerArgs pa, const FwdBake<typename Acc<T>::type> fb) {
     using A = typename Acc<T>::type;
     extern __shared__ __align__(16) unsigned char smem[];
     const int K = a.K;
     Stage<A> st = carve<A>(smem, TN, K, false);
     const int64_t j0 = (int64_t)blockIdx.x * TN;
-    fill_stage<A, false>(a, j0, TN, st);
-    if (OFF) scale_stage(st.ab, TN * K, a.ldx);
+    if (BAKED) {  // copy this CTA's part of the baked stage (entries past ns + n1 are never read)
+        const int nk = TN * K;
+        const A4<A>* __restrict__ gcf = fb.cf + j0 * K;
+        const int2* __restrict__ gab = fb.ab + j0 * K;
+        for (int e = threadIdx.x; e < nk; e += blockDim.x) {
+            st.cf[e] = gcf[e];
+            st.ab[e] = gab[e];
+        }
+        for (int t = threadIdx.x; t < TN; t += blockDim.x) {
+            st.c0[t] = fb.c0[j0 + t];
+            st.ns[t] = fb.ns[j0 + t];
+            st.n1[t] = fb.n1[j0 + t];
+        }
+    } else {
+        fill_stage<A, false>(a, j0, TN, st);
+        if (OFF) scale_stage(st.ab, TN * K, a.ldx);
+    }
     __syncthreads();
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1085,18 +1151,38 @@ int bwd_lpn(const LayerArgs& a, bool vec, int V, const void* gx, bool peers) {
 
 template <typename T, int VEC>
 void fwd_launch(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs& g, bool use_gs, dim3 grid, size_t smem,
-                int TN, cudaStream_t s, const PeerArgs& pa) {
+                int TN, cudaStream_t s, const PeerArgs& pa, void* stage) {
+    using A = typename Acc<T>::type;
+    const bool off = off32_ok(a, nullptr, 0);
+    FwdBake<A> fb{};
+    if (stage != nullptr && pa.n == 0) {
+        fb = carve_bake<A>(stage, (int64_t)grid.x * TN, a.K);
+        if (off) fwd_bake_kernel<A, true><<<grid.x, kThreads, 0, s>>>(a, TN, fb);
+        else fwd_bake_kernel<A, false><<<grid.x, kThreads, 0, s>>>(a, TN, fb);
+        auto k = off ? logic_forward_kernel<T, VEC, false, true, true> : logic_forward_kernel<T, VEC, false, false, true>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, use_gs, TN, pa, fb);
+        return;
+    }
     // the peer-store epilogue is a separate instantiation so the single-GPU kernel keeps its registers
     auto k = pa.n ? logic_forward_kernel<T, VEC, true, false>
-                  : off32_ok(a, nullptr, 0) ? logic_forward_kernel<T, VEC, false, true>
-                                            : logic_forward_kernel<T, VEC, false, false>;
+                  : off ? logic_forward_kernel<T, VEC, false, true>
+                        : logic_forward_kernel<T, VEC, false, false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, use_gs, TN, pa);
+    k<<<grid, kThreads, smem, s>>>(a, reinterpret_cast<T*>(y), ldy, g, use_gs, TN, pa, fb);
+}
+
+// Bytes of the baked forward stage of a layer (0 when the layer's forward does not use one).
+template <typename T>
+size_t fwd_stage_bytes_t(int64_t n_out, int K) {
+    using A = typename Acc<T>::type;
+    const int TN = choose_tn(stage_bytes<A>(1, K, false));
+    return bake_bytes<A>(ceil_div64(n_out, TN) * TN, K);
 }
 
 template <typename T>
 cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s,
-                  const PeerArgs& pa) {
+                  const PeerArgs& pa, void* stage) {
     using A = typename Acc<T>::type;
     const int K = a.K;
     const int TN = choose_tn(stage_bytes<A>(1, K, false));
@@ -1115,13 +1201,13 @@ cudaError_t fwd_t(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* 
                                                                                   : 32;
     if (lpn < 32) return fwd_narrow<T>(a, y, ldy, gs, lpn, s);
     if (wide) {
-        fwd_launch<T, 8>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
+        fwd_launch<T, 8>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa, stage);
     } else if (half) {
-        fwd_launch<T, 2>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
+        fwd_launch<T, 2>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa, stage);
     } else if (vec) {
-        fwd_launch<T, vmax<T>()>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
+        fwd_launch<T, vmax<T>()>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa, stage);
     } else {
-        fwd_launch<T, 1>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa);
+        fwd_launch<T, 1>(a, y, ldy, g, gs != nullptr, grid, smem, TN, s, pa, stage);
     }
     return cudaGetLastError();
 }
@@ -1217,15 +1303,25 @@ cudaError_t csr_t(const LayerArgs& a, const void* gy, int64_t ldgy, int64_t in_d
 }  // namespace
 
 cudaError_t launch_logic_forward(const LayerArgs& a, void* y, int64_t ldy, const GroupSumArgs* gs, cudaStream_t s,
-                                 const PeerArgs* peers) {
+                                 const PeerArgs* peers, void* stage) {
     const PeerArgs pa = peers ? *peers : PeerArgs{};
     switch (a.dtype) {
-        case CLB_F32: return fwd_t<float>(a, y, ldy, gs, s, pa);
-        case CLB_F64: return fwd_t<double>(a, y, ldy, gs, s, pa);
-        case CLB_BF16: return fwd_t<__nv_bfloat16>(a, y, ldy, gs, s, pa);
-        case CLB_F16: return fwd_t<__half>(a, y, ldy, gs, s, pa);
+        case CLB_F32: return fwd_t<float>(a, y, ldy, gs, s, pa, stage);
+        case CLB_F64: return fwd_t<double>(a, y, ldy, gs, s, pa, stage);
+        case CLB_BF16: return fwd_t<__nv_bfloat16>(a, y, ldy, gs, s, pa, stage);
+        case CLB_F16: return fwd_t<__half>(a, y, ldy, gs, s, pa, stage);
     }
     return cudaErrorInvalidValue;
+}
+
+size_t logic_forward_stage_bytes(int dtype, int64_t n_out, int64_t K) {
+    switch (dtype) {
+        case CLB_F32: return fwd_stage_bytes_t<float>(n_out, (int)K);
+        case CLB_F64: return fwd_stage_bytes_t<double>(n_out, (int)K);
+        case CLB_BF16: return fwd_stage_bytes_t<__nv_bfloat16>(n_out, (int)K);
+        case CLB_F16: return fwd_stage_bytes_t<__half>(n_out, (int)K);
+    }
+    return 0;
 }
 
 cudaError_t launch_logic_backward(const LayerArgs& a, const void* gy, int64_t ldgy, const GroupSumArgs* gs, void* gx,

@@ -202,6 +202,20 @@ int clb_logic_forward(int dtype, const void* x, int64_t ldx, int64_t ncols, int6
                       const uint8_t* select, int has_pad, void* y, int64_t ldy, void* gs_acc, int64_t gs_k,
                       int64_t gs_size, int64_t ld_gs, clb_stream_t stream);
 
+/* Same as clb_logic_forward, with the per-neuron stage (softmax over the K logits, gates compacted into
+ * two- and one-operand entries, scaled row offsets) computed once into `stage` (caller-allocated,
+ * 256-byte aligned, clb_logic_forward_stage_bytes bytes) instead of by every CTA of every column chunk.
+ * Native refinement of LogicLayer.forward_cuda (compactlogic.py:83-118) — the reference rebuilds nothing
+ * per chunk because its forward kernel reads logits-derived probabilities prepared by PyTorch
+ * (compactlogic.py:108).  stage == NULL behaves as clb_logic_forward; a smaller stage returns
+ * CLB_ERR_WORKSPACE.  Calls sharing one stage buffer must not overlap on the GPU. */
+size_t clb_logic_forward_stage_bytes(int dtype, int64_t n_out, int64_t K);
+int clb_logic_forward_staged(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
+                             const int32_t* slots, int64_t n_out, int64_t K, int64_t group, int weight_mode,
+                             const void* weights, const uint8_t* gates, const uint8_t* select, int has_pad, void* y,
+                             int64_t ldy, void* gs_acc, int64_t gs_k, int64_t gs_size, int64_t ld_gs, void* stage,
+                             size_t stage_bytes, clb_stream_t stream);
+
 /* Number of column chunks of the backward pass = rows of the partials scratch [nchunks, n_out, K]. */
 int64_t clb_logic_backward_chunks(int dtype, const void* x, int64_t ldx, int64_t ncols, int64_t in_features,
                                   const void* grad_y, int64_t ldgy, const void* gs_grad, int64_t ld_gs, const void* grad_x,
