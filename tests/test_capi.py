@@ -69,3 +69,15 @@ def test_gather_backward_index_sizes_and_argument_checks():
     # fp32: 128 columns per chunk when everything is 16-byte aligned, 32 (scalar) otherwise
     assert L.clb_logic_backward_gather_chunks(0, 256, 1024, 1000, 512, 1024, None, 0, 1024, 1024) == 8
     assert L.clb_logic_backward_gather_chunks(0, 256, 1023, 1000, 512, 1023, None, 0, 1024, 1024) == 32
+
+
+def test_forward_stage_sizes_and_checks():
+    """The baked forward stage's size query and argument checks (no CUDA call is made)."""
+    L = _lib.lib()
+    n = L.clb_logic_forward_stage_bytes(_lib.CLB_F32, 64000, 16)
+    assert n >= 64000 * 16 * (16 + 8) and n % 256 == 0
+    assert L.clb_logic_forward_stage_bytes(_lib.CLB_F32, 0, 16) == 0
+    assert L.clb_logic_forward_stage_bytes(9, 10, 4) == 0
+    st = L.clb_logic_forward_staged(7, None, 0, 0, 0, None, 0, 1, 1, 0, None, None, None, 0, None, 0, None, 0, 0, 0,
+                                    None, 0, None)
+    assert st == _lib.CLB_ERR_DTYPE

@@ -338,3 +338,45 @@ def test_empty_batch():
     model.eval()
     assert model(torch.zeros(0, 20, device="cuda")).shape == (0, 4)
     assert cl.PackedLogicNet(model)(torch.zeros(0, 20, device="cuda")).shape == (0, 4)
+
+
+def _fwd_call(name, xt, w, spec, mode, sel, y, gs=None, gs_size=0, stage=None):
+    args = [L.dtype_code(xt.dtype), L.ptr(xt), xt.stride(0), xt.shape[1], spec.in_features, L.ptr(spec.slots),
+            spec.n_out, spec.K, spec.group, mode, L.ptr(w), L.ptr(spec.gates), L.ptr(sel), 0,
+            L.ptr(y), y.stride(0) if y is not None else 0, L.ptr(gs), gs.shape[0] if gs is not None else 0, gs_size,
+            gs.stride(0) if gs is not None else 0]
+    if name == "clb_logic_forward_staged":
+        args += [L.ptr(stage), stage.numel() if stage is not None else 0]
+    return getattr(L.lib(), name)(*args, L.stream())
+
+
+@pytest.mark.parametrize("in_dim,out,K,B", [(784, 1000, 16, 512), (300, 517, 7, 640), (64, 96, 4, 1024)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
+def test_staged_forward_matches_per_chunk_stage(in_dim, out, K, B, dtype):
+    """clb_logic_forward_staged (stage baked once per call) gives bitwise the forward of clb_logic_forward,
+    in soft mode, select mode and with the fused GroupSum; a short stage buffer is rejected."""
+    x, a, b, logits, g, _ = rand_dense(in_dim + 3 * K, in_dim, out, K, B)
+    spec = _spec(a, b, g, in_dim)
+    xt = cuda(x, dtype)
+    w = cuda(logits, L.acc_dtype(dtype))
+    sel = cuda(O.argmax_first(logits))
+    nbytes = L.lib().clb_logic_forward_stage_bytes(L.dtype_code(dtype), out, K)
+    stage = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    for mode in (L.W_LOGITS, L.W_SELECT):
+        y0 = torch.empty(out, B, dtype=dtype, device="cuda")
+        y1 = torch.full_like(y0, float("nan"))
+        assert _fwd_call("clb_logic_forward", xt, w, spec, mode, sel, y0) == L.CLB_OK
+        assert _fwd_call("clb_logic_forward_staged", xt, w, spec, mode, sel, y1, stage=stage) == L.CLB_OK
+        torch.cuda.synchronize()
+        assert torch.equal(y0, y1), mode
+    k = 10
+    acc0 = torch.zeros(k, B, dtype=L.acc_dtype(dtype), device="cuda")
+    acc1 = torch.zeros_like(acc0)
+    size = -(-out // k)
+    assert _fwd_call("clb_logic_forward", xt, w, spec, L.W_LOGITS, None, None, acc0, size) == L.CLB_OK
+    assert _fwd_call("clb_logic_forward_staged", xt, w, spec, L.W_LOGITS, None, None, acc1, size, stage) == L.CLB_OK
+    torch.cuda.synchronize()
+    torch.testing.assert_close(acc0, acc1, rtol=1e-6, atol=1e-5)  # class sums: atomic order may differ
+    short = stage[: nbytes - 256]
+    y1 = torch.empty(out, B, dtype=dtype, device="cuda")
+    assert _fwd_call("clb_logic_forward_staged", xt, w, spec, L.W_LOGITS, sel, y1, stage=short) == L.CLB_ERR_WORKSPACE
