@@ -518,24 +518,38 @@ count_gate_pipe_kernel(const GateWords src, const int64_t rows, const int64_t nw
     pdl_wait();  // the operand rows are the previous layer's output
     if (active) {
         const uint64_t* __restrict__ xw = src.x + w;
-        for (int64_t r = r0; r < r1; r += 8) {
+        const int64_t ldx = src.ldx;
+        // one group: gather the 16 operand words of the staged tables, load the next group's tables
+        // (rows from `nx`, clamped below `r1` only near the end), evaluate the 8 gates
+        auto group = [&](int64_t nx, bool clamp, int64_t valid, uint64_t (&d)[8]) {
             uint64_t va[8], vb[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                va[q] = p[q].x >= 0 ? __ldg(xw + (int64_t)p[q].x * src.ldx) : 0ull;
-                vb[q] = p[q].y >= 0 ? __ldg(xw + (int64_t)p[q].y * src.ldx) : 0ull;
+                va[q] = p[q].x >= 0 ? __ldg(xw + (int64_t)p[q].x * ldx) : 0ull;
+                vb[q] = p[q].y >= 0 ? __ldg(xw + (int64_t)p[q].y * ldx) : 0ull;
             }
             int gc[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 gc[q] = g[q];
-                const int64_t jj = min(r + 8 + q, r1 - 1);
+                const int64_t jj = clamp ? min(nx + q, r1 - 1) : nx + q;
                 p[q] = src.ab[jj];
                 g[q] = src.gate[jj];
             }
-            uint64_t d[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) d[q] = (r + q < r1) ? gate_word<uint64_t>(gc[q], va[q], vb[q]) : 0ull;
+            for (int q = 0; q < 8; ++q) d[q] = q < valid ? gate_word<uint64_t>(gc[q], va[q], vb[q]) : 0ull;
+        };
+        int64_t r = r0;
+        // full 16-row steps whose next tables are in range: no clamping, no masking, one carry chain
+        for (; r + 24 <= r1; r += 16) {
+            uint64_t d[16];
+            group(r + 8, false, 8, *reinterpret_cast<uint64_t(*)[8]>(d));
+            group(r + 16, false, 8, *reinterpret_cast<uint64_t(*)[8]>(d + 8));
+            vc.add16(d);
+        }
+        for (; r < r1; r += 8) {
+            uint64_t d[8];
+            group(r + 8, true, r1 - r, d);
             vc.add8(d);
         }
     }
