@@ -35,6 +35,7 @@ def _grads(x, logits, spec, gy, dtype, gather, monkeypatch):
 SHAPES = [  # in, out, K, B
     (16, 24, 16, 1), (40, 30, 16, 3), (64, 64, 4, 64), (100, 80, 7, 130), (784, 512, 16, 256),
     (33, 20, 1, 8), (50, 64, 8, 96), (20, 12, 32, 40), (1000, 3, 2, 128),  # most rows read by nobody
+    (128, 1024, 16, 256), (96, 600, 8, 384),  # >= 64 occurrences per row: the 8-lanes-per-occurrence walk (fp32)
 ]
 
 
