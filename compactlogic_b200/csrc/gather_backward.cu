@@ -457,7 +457,14 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
 #pragma unroll
             for (int u = 0; u < kU2; ++u) {
                 r[u] = lds_rec<LDW>(&srec[warp][2 * ((e + u) & 31)]);
-                load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
+                if (!std::is_same<T, float>::value) {  // 16-bit rows: the unconditional load measured faster
+                    load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
+                } else if (r[u].x >= 0) {  // warp-uniform: absent other operands (zero coefficients) issue no load
+                    load_acc<T, 4>(x + r[u].x + lcol, xo[u]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) xo[u][i] = 0.f;
+                }
                 g[u] = *reinterpret_cast<const float4*>(gsrc + r[u].y + lcol);
             }
             float dot[kU2];
@@ -492,7 +499,14 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather2_kernel(
 #pragma unroll
             for (int u = 0; u < kU2; ++u) {
                 r[u] = lds_rec<LDW>(&srec[warp][2 * ((e + u) & 31)]);
-                load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
+                if (!std::is_same<T, float>::value) {  // 16-bit rows: the unconditional load measured faster
+                    load_acc<T, 4>(x + (r[u].x >= 0 ? r[u].x : rowoff) + lcol, xo[u]);
+                } else if (r[u].x >= 0) {  // warp-uniform: absent other operands (zero coefficients) issue no load
+                    load_acc<T, 4>(x + r[u].x + lcol, xo[u]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) xo[u][i] = 0.f;
+                }
                 g[u] = *reinterpret_cast<const float4*>(gsrc + r[u].y + lcol);
             }
 #pragma unroll
@@ -575,7 +589,12 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather4_kernel(
             const int o = (e + q) & 31;
             const int4 r = srec[warp][2 * o];
             float xo[C], g[C];
-            load_pieces<T>(x + (r.x >= 0 ? r.x : rowoff) + lcol, xo);
+            if (r.x >= 0) {
+                load_pieces<T>(x + r.x + lcol, xo);
+            } else {
+#pragma unroll
+                for (int i = 0; i < C; ++i) xo[i] = 0.f;
+            }
             load_pieces<float>(gsrc + r.y + lcol, g);
             const int4 cd = srec[warp][2 * o + 1];
             const float pcs = __int_as_float(r.z), pc3 = __int_as_float(r.w);
@@ -598,7 +617,12 @@ __global__ void __launch_bounds__(kThreads, MINB) logic_backward_gather4_kernel(
         for (int e = split; e < n; e += 4) {  // non-owners: grad_x only (records past n are zero records)
             const int4 r = srec[warp][2 * ((e + q) & 31)];
             float xo[C], g[C];
-            load_pieces<T>(x + (r.x >= 0 ? r.x : rowoff) + lcol, xo);
+            if (r.x >= 0) {
+                load_pieces<T>(x + r.x + lcol, xo);
+            } else {
+#pragma unroll
+                for (int i = 0; i < C; ++i) xo[i] = 0.f;
+            }
             load_pieces<float>(gsrc + r.y + lcol, g);
             const float pcs = __int_as_float(r.z), pc3 = __int_as_float(r.w);
 #pragma unroll
